@@ -1,0 +1,495 @@
+"""Benchmark of the mHC-lite hot path on B200 (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Metric: tokens/s fwd+bwd per GPU and % HBM roofline of
+K1/K3/K4 at T=65536, C=1024, n=4 (the kernel-level microbench config).  One
+step is one forward+backward pass of the hot path over a batch of T tokens:
+
+    K1 fwd -> K3 fwd -> K4 fwd -> K4 bwd -> K3 bwd -> K1 bwd (grad_x and grad_W)
+
+through ``torch.ops.flash_mhc`` (the reference's op API, each op one C-ABI
+call), on seeded synthetic inputs with the reference microbench's
+distributions (x, lo, upstream grads ~N(0,1) bf16; W ~N(0,0.02) bf16;
+h_pre/h_post/H ~N(0,1) f32).  With N > 1 (torchrun, one rank per GPU) every
+rank runs its own T-token shard (weak scaling) and the K1 weight gradient is
+all-reduced over NCCL, the path's only exchange.
+
+* ``value``: whole-job tokens/s with inputs resident in HBM (max step time over
+  ranks, CUDA events on the launching stream).  Inputs (x alone is 512 MiB)
+  exceed the 126 MB L2, so no flush is needed between steps.
+* ``roofline``: the dominant kernel (K4 backward) -- algorithmic bytes per
+  launch (the reference's bytes model, scripts/benchmark_kernels.py:64-105)
+  over its CUDA-event duration inside the timed region, against the measured
+  HBM copy bandwidth in MEASURED_PEAKS.json.
+* ``e2e``: the same step from pinned host buffers, host->device copies of every
+  input and device->host copies of every output inside the timed region.
+* ``cpu_baseline``: the CPU restatement (oracle/, float32 numpy, one process
+  per core) on a bounded token sample, rank 0 only.
+* ``--impl reference``: the reference arm.  The reference's kernels are
+  Triton-only and it has no compiled CPU implementation of this path, so the
+  arm times the CPU restatement of the reference algorithm (oracle port) with
+  all host cores on the same workload, rank 0 only.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "flash-mhc_b200"))
+sys.path.insert(0, str(ROOT))
+
+METRIC = "tokens/s fwd+bwd per GPU and % HBM roofline (K1/K3/K4) at T=65536,C=1024,n=4"
+UNIT = "tokens/s"
+D_OUT = 32
+N_STREAMS = 4
+
+
+def bytes_model(T: int, C: int, n: int = N_STREAMS, D: int = D_OUT) -> dict:
+    """Algorithmic (mandatory) HBM bytes per launch, per kernel.
+
+    The reference's model (scripts/benchmark_kernels.py:64-105) for the six
+    kernels; K1's backward here also produces grad_W, so it adds the grad_W
+    write (D*nC bf16) to the reference's K1 bwd-dx figure.
+    """
+    bf, f4 = 2, 4
+    nC = n * C
+    return {
+        "k1_fwd": T * nC * bf + D * nC * bf + T * D * bf + T * f4,
+        "k3_fwd": T * n * C * bf + T * n * f4 + T * C * bf,
+        "k4_fwd": T * n * C * bf + T * C * bf + T * n * n * f4 + T * n * f4 + T * n * C * bf,
+        "k4_bwd": 2 * T * n * C * bf + T * C * bf + T * n * n * f4 + T * n * f4
+        + T * n * C * bf + T * C * bf + T * n * n * f4 + T * n * f4,
+        "k3_bwd": T * n * C * bf + T * n * f4 + T * C * bf + T * n * C * bf + T * n * f4,
+        "k1_bwd": 2 * T * nC * bf + D * nC * bf + 2 * T * D * bf + T * f4 + D * nC * bf,
+    }
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        d = json.loads(p.read_text())
+        return {"hbm_gbs": float(d["hbm_gbs"]), "src": "measured"}
+    return {"hbm_gbs": 6650.0, "src": "fallback"}
+
+
+def dram_traffic() -> dict:
+    """Per-launch DRAM bytes per kernel from the committed ncu summary, if any."""
+    p = ROOT / "profiles" / "dram_traffic.json"
+    if p.exists():
+        return json.loads(p.read_text())
+    return {}
+
+
+# ---------------------------------------------------------------------------
+# clocks sampling (nvidia-smi during the timed region)
+# ---------------------------------------------------------------------------
+
+class ClockSampler:
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_indices):
+        self.idx = gpu_indices
+        self.proc = None
+        self.path = Path("/tmp") / f"fmhc_clocks_{os.getpid()}.csv"
+
+    def __enter__(self):
+        if not self.idx:
+            return self
+        try:
+            self.fh = open(self.path, "w")
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-i", ",".join(str(i) for i in self.idx), "-lms", "200"],
+                stdout=self.fh, stderr=subprocess.DEVNULL)
+        except Exception:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+            self.fh.close()
+
+    def summary(self) -> dict:
+        if self.proc is None or not self.path.exists():
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
+        sm, smax, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.path.read_text().splitlines():
+            f = [x.strip() for x in line.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                smax.append(float(f[2]))
+            except ValueError:
+                continue
+            for name, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
+                "samples": len(sm), "reasons": sorted(reasons)}
+
+
+# ---------------------------------------------------------------------------
+# the GPU step
+# ---------------------------------------------------------------------------
+
+class HotPath:
+    """Inputs and the fwd+bwd step of the hot path on one GPU."""
+
+    # kernels of this library launched per step: K1 fwd, K3 fwd, K4 fwd, K4 bwd,
+    # K3 bwd, K1 bwd-dx, K1 grad_W (2: split partials + reduction)
+    def __init__(self, T, C, device, seed, torch):
+        self.torch = torch
+        self.T, self.C = T, C
+        g = torch.Generator(device=device)
+        g.manual_seed(seed)
+        n, D = N_STREAMS, D_OUT
+        bf = torch.bfloat16
+
+        def rn(*shape, std=1.0, dtype=bf):
+            return (torch.randn(*shape, generator=g, device=device) * std).to(dtype)
+
+        self.inputs = {
+            "x": rn(T, n, C), "W": rn(D, n * C, std=0.02), "lo": rn(T, C),
+            "h_pre": rn(T, n, dtype=torch.float32), "h_post": rn(T, n, dtype=torch.float32),
+            "H": rn(T, n, n, dtype=torch.float32), "g_proj": rn(T, D), "g_pre": rn(T, C),
+            "g_post": rn(T, n, C),
+        }
+
+    def step(self, inp, events=None):
+        """One pass; ``events`` (dict name -> list) gets (start, end) event pairs."""
+        torch = self.torch
+        ops = torch.ops.flash_mhc
+        T, C = self.T, self.C
+        x = inp["x"]
+        xf = x.reshape(T, N_STREAMS * C)
+        outs = {}
+
+        def rec(name, fn):
+            if events is None:
+                return fn()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = fn()
+            e.record()
+            events.setdefault(name, []).append((s, e))
+            return r
+
+        outs["proj"], outs["inv_rms"] = rec("k1_fwd", lambda: ops.fused_rmsnorm_project(xf, inp["W"]))
+        outs["layer_input"] = rec("k3_fwd", lambda: ops.fused_pre_map(x, inp["h_pre"]))
+        outs["out"] = rec("k4_fwd", lambda: ops.fused_post_res(x, inp["lo"], inp["H"], inp["h_post"]))
+        (outs["gx4"], outs["glo"], outs["gH"], outs["ghp"]) = rec(
+            "k4_bwd", lambda: ops.fused_post_res_backward(inp["g_post"], x, inp["lo"], inp["H"],
+                                                          inp["h_post"]))
+        outs["gx3"], outs["gh3"] = rec(
+            "k3_bwd", lambda: ops.fused_pre_map_backward(inp["g_pre"], x, inp["h_pre"]))
+        outs["gx1"], outs["gW"] = rec(
+            "k1_bwd", lambda: ops.fused_rmsnorm_project_backward(inp["g_proj"], xf, inp["W"],
+                                                                 outs["proj"], outs["inv_rms"]))
+        return outs
+
+    LAUNCHES_PER_STEP = 8
+
+
+def _allreduce_gw(torch, dist, outs):
+    buf = outs["gW"].float()
+    dist.all_reduce(buf)
+    return buf
+
+
+def run_ours(args):
+    import torch
+    import torch.distributed as dist
+
+    import flash_mhc  # noqa: F401  (registers the ops)
+    from flash_mhc import _native
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != args.gpus:
+        raise SystemExit(f"--gpus {args.gpus} but WORLD_SIZE={world}")
+    torch.cuda.set_device(local)
+    dev = torch.device("cuda", local)
+    if world > 1:
+        from datetime import timedelta
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+
+    T, C = args.T, args.C
+    hp = HotPath(T, C, dev, seed=1234 + rank, torch=torch)
+    lib_path = str(_native.library_path())
+
+    def one_step(events=None):
+        outs = hp.step(hp.inputs, events)
+        if world > 1:
+            outs["gW_all"] = _allreduce_gw(torch, dist, outs)
+        return outs
+
+    # --- device-resident timing -------------------------------------------
+    for _ in range(args.warmup):
+        one_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    events = {}
+    phys = _physical_gpu_indices(world)
+    with ClockSampler(phys if rank == 0 else []) as clk:
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record()
+        for _ in range(args.steps):
+            one_step(events)
+        t1.record()
+        torch.cuda.synchronize()
+        if world > 1:
+            dist.barrier()
+    ms = t0.elapsed_time(t1) / args.steps
+    kern_ms = {k: sum(s.elapsed_time(e) for s, e in v) / len(v) for k, v in events.items()}
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+
+    # --- end-to-end from host buffers --------------------------------------
+    e2e = run_e2e(args, hp, one_step, torch, dist, world, dev)
+
+    if rank == 0:
+        peaks = measured_peaks()
+        bm = bytes_model(T, C)
+        traffic = dram_traffic()
+        kernels = {}
+        for k, v in kern_ms.items():
+            gbs = bm[k] / (v * 1e-3) / 1e9
+            kernels[k] = {"ms": round(v, 5), "bytes": bm[k], "GBps": round(gbs, 1),
+                          "frac": round(gbs / peaks["hbm_gbs"], 4)}
+        dom = "k4_bwd"
+        ach = bm[dom] / (kern_ms[dom] * 1e-3) / 1e9
+        tr = traffic.get(dom, {}).get("bytes_per_launch_full") if traffic else None
+        sum_bytes = sum(bm.values())
+        sum_ms = sum(kern_ms.values())
+        line = {
+            "metric": METRIC, "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT,
+            "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16",
+            "data": "synthetic (seeded N(0,1) x/lo/grads, N(0,0.02) W, N(0,1) f32 coefficients)",
+            "config": {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
+                       "T_per_gpu": T, "C": C, "n": N_STREAMS, "D": D_OUT,
+                       "step": "K1f,K3f,K4f,K4b,K3b,K1b(dx+dW)" + (",allreduce(gW)" if world > 1 else ""),
+                       "parallelism": f"token-sharded dp{world}",
+                       "l2": "inputs larger than L2 (x alone 512 MiB), no flush"},
+            "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1),
+                         "peak": peaks["hbm_gbs"], "peak_src": peaks["src"], "unit": "GB/s",
+                         "frac": round(ach / peaks["hbm_gbs"], 4),
+                         "traffic": tr, "algorithmic_bytes": bm[dom]},
+            "hot_path_hbm_frac": round(sum_bytes / (sum_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
+            "kernels": kernels,
+            "e2e": e2e,
+            "gpu_launches": HotPath.LAUNCHES_PER_STEP * args.steps,
+            "clocks": clk.summary(),
+            "native_lib": os.path.relpath(lib_path, ROOT),
+        }
+        if world == 1 and not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(args)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _physical_gpu_indices(world):
+    vis = os.environ.get("CUDA_VISIBLE_DEVICES")
+    if vis:
+        ids = [v.strip() for v in vis.split(",") if v.strip()]
+        try:
+            return [int(i) for i in ids[:world]]
+        except ValueError:
+            pass
+    return list(range(world))
+
+
+def run_e2e(args, hp, one_step, torch, dist, world, dev):
+    """Same step from pinned host memory: H2D inputs, compute, D2H outputs."""
+    host_in = {k: v.cpu().pin_memory() for k, v in hp.inputs.items()}
+    sample = hp.step(hp.inputs)
+    host_out = {k: torch.empty(v.shape, dtype=v.dtype, pin_memory=True) for k, v in sample.items()}
+    h2d = sum(v.numel() * v.element_size() for v in host_in.values())
+    d2h = sum(v.numel() * v.element_size() for v in host_out.values())
+    del sample
+
+    def e2e_step():
+        dev_in = {k: v.to(dev, non_blocking=True) for k, v in host_in.items()}
+        outs = hp.step(dev_in)
+        if world > 1:
+            outs["gW"] = _allreduce_gw(torch, dist, outs).to(outs["gW"].dtype)
+        for k, v in outs.items():
+            if k in host_out:
+                host_out[k].copy_(v, non_blocking=True)
+        return outs
+
+    steps = max(1, min(args.steps, 5))
+    for _ in range(max(1, min(args.warmup, 2))):
+        e2e_step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        e2e_step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    return {"value": round(world * hp.T / (ms * 1e-3), 1), "unit": UNIT, "ms_per_step": round(ms, 3),
+            "steps": steps, "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+            "api": "torch.ops.flash_mhc (ctypes -> C ABI), pinned host buffers"}
+
+
+# ---------------------------------------------------------------------------
+# CPU restatement (baseline and reference arm)
+# ---------------------------------------------------------------------------
+
+def _cpu_worker(args):
+    import numpy as np
+    from oracle import mhc_oracle as O
+
+    T, C, seed, reps = args
+    rng = np.random.default_rng(seed)
+    x = O.bf16_round(rng.standard_normal((T, 4, C)))
+    W = O.bf16_round(rng.standard_normal((32, 4 * C)) * 0.02)
+    lo = O.bf16_round(rng.standard_normal((T, C)))
+    H = rng.standard_normal((T, 4, 4)).astype(np.float32)
+    hq = rng.standard_normal((T, 4)).astype(np.float32)
+    hp = rng.standard_normal((T, 4)).astype(np.float32)
+    gp = O.bf16_round(rng.standard_normal((T, 32)))
+    g3 = O.bf16_round(rng.standard_normal((T, C)))
+    g4 = O.bf16_round(rng.standard_normal((T, 4, C)))
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        O.hot_path_step_f32(x, W, lo, H, hq, hp, gp, g3, g4)
+    return time.perf_counter() - t0
+
+
+class CpuPool:
+    """A spawn process pool (one process per core) running the CPU restatement."""
+
+    def __init__(self, C, workers):
+        import multiprocessing as mp
+
+        self.C, self.workers = C, workers
+        os.environ.setdefault("OMP_NUM_THREADS", "1")
+        os.environ.setdefault("OPENBLAS_NUM_THREADS", "1")
+        self.pool = mp.get_context("spawn").Pool(workers)
+        self.pool.map(_cpu_worker, [(8, C, 0, 1)] * workers)  # imports, first touch
+
+    def run(self, tokens_per_worker, reps, seed=100):
+        """(tokens/s, wall s) of every worker running ``reps`` steps of its tokens."""
+        t0 = time.perf_counter()
+        self.pool.map(_cpu_worker, [(tokens_per_worker, self.C, seed + i, reps)
+                                    for i in range(self.workers)])
+        wall = time.perf_counter() - t0
+        return self.workers * tokens_per_worker * reps / wall, wall
+
+    def close(self):
+        self.pool.close()
+        self.pool.join()
+
+
+def cpu_baseline(args):
+    cores = len(os.sched_getaffinity(0))
+    tpw, reps = args.cpu_tokens_per_worker, args.cpu_reps
+    pool = CpuPool(args.C, cores)
+    try:
+        tps, wall = pool.run(tpw, reps)
+    finally:
+        pool.close()
+    return {"value": round(tps, 1), "unit": UNIT, "cores": cores, "kind": "port",
+            "sample": f"{cores} spawn processes x {reps} steps x {tpw} tokens (C={args.C}, n=4) "
+                      f"of the float32 CPU restatement, {wall:.1f} s wall"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    cores = len(os.sched_getaffinity(0))
+    tpw = args.cpu_tokens_per_worker
+    pool = CpuPool(args.C, cores)
+    try:
+        for i in range(args.warmup):
+            pool.run(64, 1, seed=10 + i)
+        times = [pool.run(tpw, 1, seed=1000 + 97 * i)[1] for i in range(args.steps)]
+    finally:
+        pool.close()
+    tok = cores * tpw
+    ms = 1e3 * sum(times) / len(times)
+    value = tok / (ms * 1e-3)
+    line = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
+        "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
+        "config": {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
+                   "T_per_gpu": args.T, "C": args.C, "n": N_STREAMS, "D": D_OUT,
+                   "sample_tokens_per_step": tok},
+        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": "port",
+                         "sample": f"{tok} of the {args.T} tokens per step ({cores} spawn "
+                                   f"processes x {tpw}), float32 CPU restatement of the "
+                                   "reference algorithm (the reference has no compiled CPU path)"},
+        "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
+                "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--T", type=int, default=65536, help="tokens per GPU")
+    ap.add_argument("--C", type=int, default=1024)
+    ap.add_argument("--cpu-tokens-per-worker", type=int, default=1024)
+    ap.add_argument("--cpu-reps", type=int, default=4)
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and args.impl == "ours":
+        print("note: the timing rules ask for >= 3 warm-up steps", file=sys.stderr)
+    if args.impl == "reference":
+        run_reference(args)
+    else:
+        run_ours(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,207 @@
+// C ABI (include/flashmhc.h): argument validation, path selection, launch,
+// error reporting.  No device memory is allocated here.
+#include <cstdarg>
+#include <cstdio>
+
+#include "../../include/flashmhc.h"
+#include "fmhc_launch.h"
+#include "k1_tc.h"
+
+namespace {
+
+thread_local char g_err[512] = "";
+
+int fail(int code, const char *fmt, ...) {
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(g_err, sizeof(g_err), fmt, ap);
+  va_end(ap);
+  return code;
+}
+
+int ok() {
+  g_err[0] = '\0';
+  return FMHC_OK;
+}
+
+int check_launch(const char *what) {
+  cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return fail(FMHC_ERR_LAUNCH, "%s: launch failed: %s", what, cudaGetErrorString(e));
+  return ok();
+}
+
+bool aligned(const void *p, uintptr_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+// Largest bf16 chunk width v in {8,4,2,1} with C % v == 0 and every bf16
+// pointer aligned to 2*v bytes.
+int pick_vec(int64_t C, std::initializer_list<const void *> ptrs) {
+  for (int v : {8, 4, 2, 1}) {
+    if (C % v) continue;
+    bool good = true;
+    for (const void *p : ptrs) good = good && aligned(p, uintptr_t(2 * v));
+    if (good) return v;
+  }
+  return 0;
+}
+
+int check_streams(const char *what, int64_t T, int64_t n, int64_t C) {
+  if (T < 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: T must be >= 0 (got %lld)", what, (long long)T);
+  if (n != 4) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: supports n=4 only (got n=%lld)", what, (long long)n);
+  if (C < 1 || C > (int64_t(1) << 28))
+    return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: C must be in [1, 2^28] (got %lld)", what, (long long)C);
+  return FMHC_OK;
+}
+
+#define FMHC_REQUIRE_PTR(what, p) \
+  if ((p) == nullptr) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: %s is NULL", what, #p)
+#define FMHC_REQUIRE_ALIGN16(what, p) \
+  if (!aligned((p), 16)) return fail(FMHC_ERR_ALIGNMENT, "%s: %s must be 16-byte aligned", what, #p)
+#define FMHC_REQUIRE_ALIGN2(what, p) \
+  if (!aligned((p), 2)) return fail(FMHC_ERR_ALIGNMENT, "%s: %s must be 2-byte aligned", what, #p)
+
+}  // namespace
+
+extern "C" {
+
+const char *fmhc_last_error(void) { return g_err; }
+
+const char *fmhc_version(void) { return "flashmhc-sm100 0.1.0"; }
+
+int fmhc_k3_fwd(const void *x, const float *h_pre, void *out, int64_t T, int64_t n, int64_t C,
+                void *stream) {
+  const char *w = "fmhc_k3_fwd";
+  if (int e = check_streams(w, T, n, C)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, h_pre); FMHC_REQUIRE_PTR(w, out);
+  FMHC_REQUIRE_ALIGN16(w, h_pre);
+  FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, out);
+  const int vec = pick_vec(C, {x, out});
+  fmhc::launch_k3_fwd(x, h_pre, out, T, int(C), vec, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int fmhc_k3_bwd(const void *grad_out, const void *x, const float *h_pre, void *grad_x,
+                float *grad_h, int64_t T, int64_t n, int64_t C, void *stream) {
+  const char *w = "fmhc_k3_bwd";
+  if (int e = check_streams(w, T, n, C)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, h_pre);
+  FMHC_REQUIRE_PTR(w, grad_x); FMHC_REQUIRE_PTR(w, grad_h);
+  FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, grad_h);
+  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, grad_x);
+  const int vec = pick_vec(C, {grad_out, x, grad_x});
+  fmhc::launch_k3_bwd(grad_out, x, h_pre, grad_x, grad_h, T, int(C), vec, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int fmhc_k4_fwd(const void *x, const void *lo, const float *H, const float *h_post, void *out,
+                int64_t T, int64_t n, int64_t C, void *stream) {
+  const char *w = "fmhc_k4_fwd";
+  if (int e = check_streams(w, T, n, C)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, lo); FMHC_REQUIRE_PTR(w, H);
+  FMHC_REQUIRE_PTR(w, h_post); FMHC_REQUIRE_PTR(w, out);
+  FMHC_REQUIRE_ALIGN16(w, H); FMHC_REQUIRE_ALIGN16(w, h_post);
+  FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, lo); FMHC_REQUIRE_ALIGN2(w, out);
+  const int vec = pick_vec(C, {x, lo, out});
+  fmhc::launch_k4_fwd(x, lo, H, h_post, out, T, int(C), vec, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int fmhc_k4_bwd(const void *grad_out, const void *x, const void *lo, const float *H,
+                const float *h_post, void *grad_x, void *grad_lo, float *grad_H,
+                float *grad_hp, int64_t T, int64_t n, int64_t C, void *stream) {
+  const char *w = "fmhc_k4_bwd";
+  if (int e = check_streams(w, T, n, C)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, lo);
+  FMHC_REQUIRE_PTR(w, H); FMHC_REQUIRE_PTR(w, h_post); FMHC_REQUIRE_PTR(w, grad_x);
+  FMHC_REQUIRE_PTR(w, grad_lo); FMHC_REQUIRE_PTR(w, grad_H); FMHC_REQUIRE_PTR(w, grad_hp);
+  FMHC_REQUIRE_ALIGN16(w, H); FMHC_REQUIRE_ALIGN16(w, h_post);
+  FMHC_REQUIRE_ALIGN16(w, grad_H); FMHC_REQUIRE_ALIGN16(w, grad_hp);
+  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, lo);
+  FMHC_REQUIRE_ALIGN2(w, grad_x); FMHC_REQUIRE_ALIGN2(w, grad_lo);
+  const int vec = pick_vec(C, {grad_out, x, lo, grad_x, grad_lo});
+  fmhc::launch_k4_bwd(grad_out, x, lo, H, h_post, grad_x, grad_lo, grad_H, grad_hp, T, int(C),
+                      vec, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+static int check_k1(const char *w, int64_t T, int64_t nC, int64_t D) {
+  if (T < 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: T must be >= 0 (got %lld)", w, (long long)T);
+  if (nC < 1 || nC > (int64_t(1) << 28))
+    return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: nC must be in [1, 2^28] (got %lld)", w, (long long)nC);
+  if (D < 1 || D > 32)
+    return fail(FMHC_ERR_UNSUPPORTED, "%s: D (projection width) must be in [1, 32] (got %lld)", w,
+                (long long)D);
+  return FMHC_OK;
+}
+
+int fmhc_k1_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t T, int64_t nC,
+                int64_t D, void *stream) {
+  const char *w = "fmhc_k1_fwd";
+  if (int e = check_k1(w, T, nC, D)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, W); FMHC_REQUIRE_PTR(w, out);
+  FMHC_REQUIRE_PTR(w, inv_rms);
+  FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, W); FMHC_REQUIRE_ALIGN2(w, out);
+  if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (fmhc::k1_tc_fwd_supported(x, W, out, inv_rms, T, nC, D)) {
+    if (int e = fmhc::launch_k1_tc_fwd(x, W, out, inv_rms, T, int(nC), s))
+      return fail(e, "%s: %s", w, fmhc::k1_tc_error());
+  } else {
+    const int vec = pick_vec(nC, {x, W});
+    fmhc::launch_k1_fwd_simt(x, W, out, inv_rms, T, int(nC), int(D), vec == 8 ? 8 : 1, s);
+  }
+  return check_launch(w);
+}
+
+int fmhc_k1_bwd_dx(const void *grad_out, const void *x, const void *W, const void *proj,
+                   const float *inv_rms, void *grad_x, int64_t T, int64_t nC, int64_t D,
+                   void *stream) {
+  const char *w = "fmhc_k1_bwd_dx";
+  if (int e = check_k1(w, T, nC, D)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, W);
+  FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, inv_rms); FMHC_REQUIRE_PTR(w, grad_x);
+  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, W);
+  FMHC_REQUIRE_ALIGN2(w, proj); FMHC_REQUIRE_ALIGN2(w, grad_x);
+  if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
+  const int vec = pick_vec(nC, {x, W, grad_x});
+  fmhc::launch_k1_bwd_dx_simt(grad_out, x, W, proj, inv_rms, grad_x, T, int(nC), int(D),
+                              vec == 8 ? 8 : 1, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int64_t fmhc_k1_bwd_dw_workspace_size(int64_t T, int64_t nC, int64_t D) {
+  if (T <= 0 || nC <= 0 || D <= 0) return 0;
+  return fmhc::k1_dw_workspace_bytes(T, nC, D);
+}
+
+int fmhc_k1_bwd_dw(const void *grad_out, const void *x, const float *inv_rms, void *grad_W,
+                   void *workspace, int64_t workspace_bytes, int64_t T, int64_t nC, int64_t D,
+                   void *stream) {
+  const char *w = "fmhc_k1_bwd_dw";
+  if (int e = check_k1(w, T, nC, D)) return e;
+  FMHC_REQUIRE_PTR(w, grad_W);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (T == 0) {
+    // Empty batch: the gradient is exactly zero.
+    if (cudaMemsetAsync(grad_W, 0, size_t(D * nC) * 2, s) != cudaSuccess)
+      return fail(FMHC_ERR_CUDA, "%s: cudaMemsetAsync failed", w);
+    return ok();
+  }
+  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, inv_rms);
+  FMHC_REQUIRE_PTR(w, workspace);
+  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, grad_W);
+  if (!aligned(workspace, 256)) return fail(FMHC_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", w);
+  const int64_t need = fmhc::k1_dw_workspace_bytes(T, nC, D);
+  if (workspace_bytes < need)
+    return fail(FMHC_ERR_WORKSPACE, "%s: workspace of %lld bytes, %lld needed", w,
+                (long long)workspace_bytes, (long long)need);
+  fmhc::launch_k1_dw_simt(grad_out, x, inv_rms, grad_W, (float *)workspace, T, int(nC), int(D), s);
+  return check_launch(w);
+}
+
+}  // extern "C"

@@ -1,0 +1,32 @@
+// Internal (C++) launchers behind the C ABI in include/flashmhc.h.  They assume
+// the arguments were validated by capi.cu and only enqueue kernels.
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fmhc {
+
+// k3k4_stream.cu -- `vec` is the bf16 chunk width (8, 4, 2 or 1).
+void launch_k3_fwd(const void *x, const float *hp, void *out, int64_t T, int C, int vec,
+                   cudaStream_t s);
+void launch_k3_bwd(const void *go, const void *x, const float *hp, void *gx, float *gh,
+                   int64_t T, int C, int vec, cudaStream_t s);
+void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *hp, void *out,
+                   int64_t T, int C, int vec, cudaStream_t s);
+void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H,
+                   const float *hp, void *gx, void *glo, float *gH, float *ghp, int64_t T,
+                   int C, int vec, cudaStream_t s);
+
+// k1_simt.cu -- general-shape K1 (vec is 8 or 1).
+void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
+                        int nC, int D, int vec, cudaStream_t s);
+void launch_k1_bwd_dx_simt(const void *go, const void *x, const void *W, const void *proj,
+                           const float *inv_rms, void *gx, int64_t T, int nC, int D, int vec,
+                           cudaStream_t s);
+int k1_dw_splits(int64_t T);
+int64_t k1_dw_workspace_bytes(int64_t T, int64_t nC, int64_t D);
+void launch_k1_dw_simt(const void *go, const void *x, const float *inv_rms, void *gW,
+                       float *ws, int64_t T, int nC, int D, cudaStream_t s);
+
+}  // namespace fmhc

@@ -1,0 +1,237 @@
+// K1 (fused RMSNorm + thin projection) on the CUDA cores.
+//
+// These kernels cover every shape (any nC, D <= 32, any T) and are the
+// general path; the tensor-core kernels in k1_tc.cu take the shapes they
+// support.  One warp owns one token row; lanes walk nC in VEC-wide chunks.
+//
+//   fwd : inv_rms[t] = rsqrt(sum_k x^2 / nC + 1e-6); out[t,d] = bf16(acc_d * inv_rms)
+//         (src/flash_mhc/kernels.py:250-303)
+//   dx  : gx = bf16(inv_rms * (go @ W) - (go . proj) * inv_rms^2 / nC * x)
+//         (src/flash_mhc/kernels.py:306-376)
+//   dW  : gW = bf16(sum_t bf16(go * inv_rms) x), two kernels: per-split f32
+//         partial sums into caller workspace, then a fixed-order reduction
+//         (deterministic), replacing src/flash_mhc/ops.py:683-684.
+#include "fmhc_common.cuh"
+#include "fmhc_launch.h"
+
+namespace fmhc {
+
+using bf16 = __nv_bfloat16;
+constexpr float kK1Eps = 1e-6f;
+
+template <int VEC>
+__global__ void __launch_bounds__(256)
+k1_fwd_simt_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
+                   bf16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T, int nC,
+                   int D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int nchunk = nC / VEC;
+  for (int64_t t = warp; t < T; t += nwarps) {
+    const bf16 *xr = x + t * nC;
+    float acc[32];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) acc[d] = 0.f;
+    float ss = 0.f;
+    for (int c = lane; c < nchunk; c += 32) {
+      float fx[VEC];
+      load_stream<VEC>(xr + c * VEC, fx);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) ss = fmaf(fx[e], fx[e], ss);
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        if (d < D) {
+          float fw[VEC];
+          // W is small and shared by every token: keep it in the caches.
+          if constexpr (VEC == 8) {
+            uint4 u = __ldg(reinterpret_cast<const uint4 *>(W + int64_t(d) * nC + c * VEC));
+            fw[0] = bf16lo(u.x); fw[1] = bf16hi(u.x); fw[2] = bf16lo(u.y); fw[3] = bf16hi(u.y);
+            fw[4] = bf16lo(u.z); fw[5] = bf16hi(u.z); fw[6] = bf16lo(u.w); fw[7] = bf16hi(u.w);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) fw[e] = __bfloat162float(W[int64_t(d) * nC + c * VEC + e]);
+          }
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) acc[d] = fmaf(fx[e], fw[e], acc[d]);
+        }
+      }
+    }
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) ss += __shfl_xor_sync(0xffffffffu, ss, off);
+    const float r = rsqrtf(ss / float(nC) + kK1Eps);
+    warp_reduce_scatter<32>(acc, lane);
+    const int d = scatter_index<32>(lane);
+    if (d < D) out[t * D + d] = __float2bfloat16_rn(acc[0] * r);
+    if (lane == 0) inv_rms[t] = r;
+  }
+}
+
+template <int VEC>
+__global__ void __launch_bounds__(256)
+k1_bwd_dx_simt_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
+                      const bf16 *__restrict__ W, const bf16 *__restrict__ proj,
+                      const float *__restrict__ inv_rms, bf16 *__restrict__ gx, int64_t T,
+                      int nC, int D) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int nchunk = nC / VEC;
+  for (int64_t t = warp; t < T; t += nwarps) {
+    const float r = inv_rms[t];
+    float g_l = 0.f, p_l = 0.f;
+    if (lane < D) {
+      g_l = __bfloat162float(go[t * D + lane]);
+      p_l = __bfloat162float(proj[t * D + lane]);
+    }
+    float dot = g_l * p_l;
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) dot += __shfl_xor_sync(0xffffffffu, dot, off);
+    const float s = dot * (r * r) / float(nC);
+    float gd[32];
+#pragma unroll
+    for (int d = 0; d < 32; ++d) gd[d] = __shfl_sync(0xffffffffu, g_l, d);
+    const bf16 *xr = x + t * nC;
+    bf16 *gr = gx + t * nC;
+    for (int c = lane; c < nchunk; c += 32) {
+      float o[VEC];
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = 0.f;
+#pragma unroll
+      for (int d = 0; d < 32; ++d) {
+        if (d < D) {
+          float fw[VEC];
+          if constexpr (VEC == 8) {
+            uint4 u = __ldg(reinterpret_cast<const uint4 *>(W + int64_t(d) * nC + c * VEC));
+            fw[0] = bf16lo(u.x); fw[1] = bf16hi(u.x); fw[2] = bf16lo(u.y); fw[3] = bf16hi(u.y);
+            fw[4] = bf16lo(u.z); fw[5] = bf16hi(u.z); fw[6] = bf16lo(u.w); fw[7] = bf16hi(u.w);
+          } else {
+#pragma unroll
+            for (int e = 0; e < VEC; ++e) fw[e] = __bfloat162float(W[int64_t(d) * nC + c * VEC + e]);
+          }
+#pragma unroll
+          for (int e = 0; e < VEC; ++e) o[e] = fmaf(gd[d], fw[e], o[e]);
+        }
+      }
+      float fx[VEC];
+      load_stream<VEC>(xr + c * VEC, fx);
+#pragma unroll
+      for (int e = 0; e < VEC; ++e) o[e] = r * o[e] - s * fx[e];
+      store_stream<VEC>(gr + c * VEC, o);
+    }
+  }
+}
+
+// dW partial sums: block (256 threads) owns 256 consecutive columns k and one
+// token split; the split's scaled grads bf16(go*inv_rms) are staged 32 tokens
+// at a time in shared memory.  ws layout: [split][d][k] f32.
+constexpr int kDwTile = 32;
+__global__ void __launch_bounds__(256)
+k1_dw_partial_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
+                     const float *__restrict__ inv_rms, float *__restrict__ ws, int64_t T,
+                     int nC, int D, int64_t tokens_per_split) {
+  __shared__ float gos[kDwTile][32];
+  const int k = blockIdx.x * 256 + threadIdx.x;
+  const int split = blockIdx.y;
+  const int64_t t0 = int64_t(split) * tokens_per_split;
+  int64_t t1 = t0 + tokens_per_split;
+  if (t1 > T) t1 = T;
+  float acc[32];
+#pragma unroll
+  for (int d = 0; d < 32; ++d) acc[d] = 0.f;
+  for (int64_t tb = t0; tb < t1; tb += kDwTile) {
+    __syncthreads();
+    for (int i = threadIdx.x; i < kDwTile * 32; i += 256) {
+      const int tt = i / 32, d = i % 32;
+      const int64_t t = tb + tt;
+      float v = 0.f;
+      if (t < t1 && d < D) {
+        v = __bfloat162float(go[t * D + d]) * inv_rms[t];
+        v = __bfloat162float(__float2bfloat16_rn(v));  // the reference rounds to bf16
+      }
+      gos[tt][d] = v;
+    }
+    __syncthreads();
+    if (k < nC) {
+      const int nt = int((t1 - tb) < kDwTile ? (t1 - tb) : kDwTile);
+      for (int tt = 0; tt < nt; ++tt) {
+        const float xv = __bfloat162float(x[(tb + tt) * nC + k]);
+#pragma unroll
+        for (int d = 0; d < 32; ++d) acc[d] = fmaf(gos[tt][d], xv, acc[d]);
+      }
+    }
+  }
+  if (k < nC) {
+    for (int d = 0; d < D; ++d) ws[(int64_t(split) * D + d) * nC + k] = acc[d];
+  }
+}
+
+__global__ void k1_dw_reduce_kernel(const float *__restrict__ ws, bf16 *__restrict__ gW,
+                                    int nsplit, int64_t n) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= n) return;
+  float s = 0.f;
+  for (int p = 0; p < nsplit; ++p) s += ws[int64_t(p) * n + i];
+  gW[i] = __float2bfloat16_rn(s);
+}
+
+int k1_dw_splits(int64_t T) {
+  int64_t s = (T + 1023) / 1024;
+  if (s < 1) s = 1;
+  if (s > 64) s = 64;
+  return int(s);
+}
+
+int64_t k1_dw_workspace_bytes(int64_t T, int64_t nC, int64_t D) {
+  return int64_t(k1_dw_splits(T)) * D * nC * int64_t(sizeof(float));
+}
+
+namespace {
+int sm_count() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+int warp_grid(int64_t T) {
+  const int64_t cap = int64_t(sm_count()) * 8;  // 8 blocks of 8 warps per SM
+  const int64_t need = (T + 7) / 8;
+  return int(need < cap ? need : cap);
+}
+}  // namespace
+
+void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
+                        int nC, int D, int vec, cudaStream_t s) {
+  if (vec == 8)
+    k1_fwd_simt_kernel<8><<<warp_grid(T), 256, 0, s>>>((const bf16 *)x, (const bf16 *)W,
+                                                       (bf16 *)out, inv_rms, T, nC, D);
+  else
+    k1_fwd_simt_kernel<1><<<warp_grid(T), 256, 0, s>>>((const bf16 *)x, (const bf16 *)W,
+                                                       (bf16 *)out, inv_rms, T, nC, D);
+}
+
+void launch_k1_bwd_dx_simt(const void *go, const void *x, const void *W, const void *proj,
+                           const float *inv_rms, void *gx, int64_t T, int nC, int D, int vec,
+                           cudaStream_t s) {
+  if (vec == 8)
+    k1_bwd_dx_simt_kernel<8><<<warp_grid(T), 256, 0, s>>>(
+        (const bf16 *)go, (const bf16 *)x, (const bf16 *)W, (const bf16 *)proj, inv_rms,
+        (bf16 *)gx, T, nC, D);
+  else
+    k1_bwd_dx_simt_kernel<1><<<warp_grid(T), 256, 0, s>>>(
+        (const bf16 *)go, (const bf16 *)x, (const bf16 *)W, (const bf16 *)proj, inv_rms,
+        (bf16 *)gx, T, nC, D);
+}
+
+void launch_k1_dw_simt(const void *go, const void *x, const float *inv_rms, void *gW,
+                       float *ws, int64_t T, int nC, int D, cudaStream_t s) {
+  const int nsplit = k1_dw_splits(T);
+  const int64_t per = (T + nsplit - 1) / nsplit;
+  dim3 grid((nC + 255) / 256, nsplit);
+  k1_dw_partial_kernel<<<grid, 256, 0, s>>>((const bf16 *)go, (const bf16 *)x, inv_rms, ws, T,
+                                            nC, D, per);
+  const int64_t n = int64_t(D) * nC;
+  k1_dw_reduce_kernel<<<int((n + 255) / 256), 256, 0, s>>>(ws, (bf16 *)gW, nsplit, n);
+}
+
+}  // namespace fmhc

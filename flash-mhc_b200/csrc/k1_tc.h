@@ -1,0 +1,18 @@
+// K1 on the 5th-generation tensor cores (TMA + tcgen05.mma + TMEM).
+#pragma once
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+namespace fmhc {
+
+// True when the tensor-core forward kernel handles this call (shape, alignment,
+// device).  Otherwise the CUDA-core kernel in k1_simt.cu runs.
+bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
+                         int64_t T, int64_t nC, int64_t D);
+// Returns 0 or an fmhc_status code; k1_tc_error() then describes the failure.
+int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t T, int nC,
+                     cudaStream_t s);
+const char *k1_tc_error();
+
+}  // namespace fmhc

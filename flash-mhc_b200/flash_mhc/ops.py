@@ -1,0 +1,354 @@
+"""torch.library custom ops of mHC-lite, backed by the sm_100a C-ABI library.
+
+The op namespace, the six schemas, the fake (meta) implementations and the
+autograd formulas are those of the reference (src/flash_mhc/ops.py:22-41,
+145-202, 670-714), so this module is a drop-in: ``torch.ops.flash_mhc.*``
+calls, ``torch.compile`` tracing through the fakes, and autograd all behave
+as before.  The CUDA implementations allocate the outputs with torch, pass raw
+pointers and the current CUDA stream to ``libflashmhc_sm100.so`` and raise on
+a non-zero status.  There is no CPU kernel (as in the reference: the ops raise
+on CPU tensors) and no fallback when the library is missing.
+
+Added beyond the reference: ``fused_rmsnorm_project_backward`` computes K1's
+grad_x AND grad_W in one op; K1's autograd formula uses it instead of the
+reference's separate cuBLAS matmul (src/flash_mhc/ops.py:683-684).
+"""
+
+from __future__ import annotations
+
+import os
+import threading
+from contextlib import contextmanager
+
+import torch
+import torch.library
+
+from . import _native
+
+_lib = torch.library.Library("flash_mhc", "DEF")
+
+_lib.define(
+    "fused_rmsnorm_project(Tensor x_flat, Tensor W) -> (Tensor out, Tensor inv_rms)"
+)
+_lib.define(
+    "fused_rmsnorm_project_bwd_dx(Tensor grad_out, Tensor x_flat, Tensor W, Tensor proj_out, Tensor inv_rms) -> Tensor grad_x"
+)
+_lib.define("fused_pre_map(Tensor x_streams, Tensor h_pre) -> Tensor out")
+_lib.define(
+    "fused_pre_map_backward(Tensor grad_out, Tensor x_streams, Tensor h_pre) -> (Tensor grad_x, Tensor grad_h_pre)"
+)
+_lib.define(
+    "fused_post_res(Tensor x_streams, Tensor layer_output, Tensor H_merged, Tensor h_post) -> Tensor out"
+)
+_lib.define(
+    "fused_post_res_backward(Tensor grad_out, Tensor x_streams, Tensor layer_output, Tensor H_merged, Tensor h_post) -> (Tensor grad_x, Tensor grad_layer_output, Tensor grad_H_merged, Tensor grad_h_post)"
+)
+# Not in the reference: K1 grad_x and grad_W together.
+_lib.define(
+    "fused_rmsnorm_project_backward(Tensor grad_out, Tensor x_flat, Tensor W, Tensor proj_out, Tensor inv_rms) -> (Tensor grad_x, Tensor grad_W)"
+)
+
+# ---------------------------------------------------------------------------
+# Autotune controls.  The reference exposes a thread-local context manager and
+# environment switches for its Triton autotuner (src/flash_mhc/ops.py:44-68).
+# The CUDA kernels here have fixed, shape-derived launch configurations and no
+# runtime search; the API is kept so callers keep working, and it changes
+# nothing.
+# ---------------------------------------------------------------------------
+_AUTOTUNE_CONTROL = threading.local()
+
+
+def _autotune_disable_depth() -> int:
+    return int(getattr(_AUTOTUNE_CONTROL, "disable_depth", 0))
+
+
+@contextmanager
+def disable_autotune_temporarily():
+    """Kept for API compatibility; launch configurations are fixed (no autotune)."""
+    _AUTOTUNE_CONTROL.disable_depth = _autotune_disable_depth() + 1
+    try:
+        yield
+    finally:
+        _AUTOTUNE_CONTROL.disable_depth = max(0, _autotune_disable_depth() - 1)
+
+
+def _autotune_enabled() -> bool:
+    """Mirrors the reference switch (FLASH_MHC_TRITON_AUTOTUNE); informational only."""
+    v = os.getenv("FLASH_MHC_TRITON_AUTOTUNE", "1").strip().lower()
+    return v not in {"0", "false", "off", "no"} and _autotune_disable_depth() == 0
+
+
+# ---------------------------------------------------------------------------
+# Fake implementations (shapes/dtypes identical to src/flash_mhc/ops.py:145-202)
+# ---------------------------------------------------------------------------
+
+
+@torch.library.register_fake("flash_mhc::fused_rmsnorm_project")
+def _fused_rmsnorm_project_fake(x_flat: torch.Tensor, W: torch.Tensor):
+    T = x_flat.shape[0]
+    D_out = W.shape[0]
+    out = torch.empty((T, D_out), device=x_flat.device, dtype=x_flat.dtype)
+    inv_rms = torch.empty((T,), device=x_flat.device, dtype=torch.float32)
+    return out, inv_rms
+
+
+@torch.library.register_fake("flash_mhc::fused_rmsnorm_project_bwd_dx")
+def _fused_rmsnorm_project_bwd_dx_fake(grad_out, x_flat, W, proj_out, inv_rms):
+    return torch.empty_like(x_flat)
+
+
+@torch.library.register_fake("flash_mhc::fused_rmsnorm_project_backward")
+def _fused_rmsnorm_project_backward_fake(grad_out, x_flat, W, proj_out, inv_rms):
+    return torch.empty_like(x_flat), torch.empty_like(W, dtype=x_flat.dtype)
+
+
+@torch.library.register_fake("flash_mhc::fused_pre_map")
+def _fused_pre_map_fake(x_streams: torch.Tensor, h_pre: torch.Tensor):
+    T, _, C = x_streams.shape
+    return torch.empty((T, C), device=x_streams.device, dtype=x_streams.dtype)
+
+
+@torch.library.register_fake("flash_mhc::fused_pre_map_backward")
+def _fused_pre_map_backward_fake(grad_out, x_streams, h_pre):
+    grad_x = torch.empty_like(x_streams)
+    grad_h_pre = torch.empty_like(h_pre, dtype=torch.float32)
+    return grad_x, grad_h_pre
+
+
+@torch.library.register_fake("flash_mhc::fused_post_res")
+def _fused_post_res_fake(x_streams, layer_output, H_merged, h_post):
+    return torch.empty_like(x_streams)
+
+
+@torch.library.register_fake("flash_mhc::fused_post_res_backward")
+def _fused_post_res_backward_fake(grad_out, x_streams, layer_output, H_merged, h_post):
+    grad_x = torch.empty_like(x_streams)
+    grad_layer_output = torch.empty_like(layer_output)
+    grad_H_merged = torch.empty_like(H_merged, dtype=torch.float32)
+    grad_h_post = torch.empty_like(h_post, dtype=torch.float32)
+    return grad_x, grad_layer_output, grad_H_merged, grad_h_post
+
+
+# ---------------------------------------------------------------------------
+# CUDA implementations
+# ---------------------------------------------------------------------------
+
+
+def _stream(t: torch.Tensor) -> int:
+    return torch.cuda.current_stream(t.device).cuda_stream
+
+
+def _bf16(name: str, t: torch.Tensor) -> torch.Tensor:
+    if t.dtype != torch.bfloat16:
+        raise ValueError(f"flash_mhc: {name} must be bfloat16 (got {t.dtype})")
+    return t.contiguous()
+
+
+def _coef(t: torch.Tensor) -> torch.Tensor:
+    """Small f32 coefficient tensors: contiguous, float32, 16-byte aligned."""
+    t = t.to(torch.float32).contiguous()
+    if t.data_ptr() % 16:
+        t = t.clone()
+    return t
+
+
+def _n4(op: str, n: int) -> None:
+    if n != 4:
+        raise ValueError(f"flash_mhc::{op} currently supports n=4 only")
+
+
+class _on_device:
+    """Make ``t``'s device current for the duration of a C-ABI call."""
+
+    __slots__ = ("idx", "prev")
+
+    def __init__(self, t: torch.Tensor):
+        self.idx = t.device.index
+
+    def __enter__(self):
+        self.prev = torch.cuda.current_device()
+        if self.idx is not None and self.idx != self.prev:
+            torch.cuda.set_device(self.idx)
+
+    def __exit__(self, *exc):
+        if self.idx is not None and self.idx != self.prev:
+            torch.cuda.set_device(self.prev)
+
+
+@torch.library.impl(_lib, "fused_rmsnorm_project", "CUDA")
+def _fused_rmsnorm_project_cuda(x_flat: torch.Tensor, W: torch.Tensor):
+    x_flat = _bf16("x_flat", x_flat)
+    W = _bf16("W", W)
+    T, nC = x_flat.shape
+    D_out = W.shape[0]
+    if W.shape[1] != nC:
+        raise ValueError(f"flash_mhc::fused_rmsnorm_project: W is {tuple(W.shape)}, x_flat has nC={nC}")
+    out = torch.empty((T, D_out), device=x_flat.device, dtype=x_flat.dtype)
+    inv_rms = torch.empty((T,), device=x_flat.device, dtype=torch.float32)
+    with _on_device(x_flat):
+        _native.call("fmhc_k1_fwd", x_flat.data_ptr(), W.data_ptr(), out.data_ptr(),
+                     inv_rms.data_ptr(), T, nC, D_out, _stream(x_flat))
+    return out, inv_rms
+
+
+@torch.library.impl(_lib, "fused_rmsnorm_project_bwd_dx", "CUDA")
+def _fused_rmsnorm_project_bwd_dx_cuda(grad_out, x_flat, W, proj_out, inv_rms):
+    grad_out = _bf16("grad_out", grad_out)
+    x_flat = _bf16("x_flat", x_flat)
+    W = _bf16("W", W)
+    proj_out = _bf16("proj_out", proj_out)
+    inv_rms = inv_rms.to(torch.float32).contiguous()
+    T, nC = x_flat.shape
+    D_out = W.shape[0]
+    grad_x = torch.empty_like(x_flat)
+    with _on_device(x_flat):
+        _native.call("fmhc_k1_bwd_dx", grad_out.data_ptr(), x_flat.data_ptr(), W.data_ptr(),
+                     proj_out.data_ptr(), inv_rms.data_ptr(), grad_x.data_ptr(), T, nC, D_out,
+                     _stream(x_flat))
+    return grad_x
+
+
+def _k1_grad_w(grad_out, x_flat, inv_rms, D_out):
+    T, nC = x_flat.shape
+    grad_W = torch.empty((D_out, nC), device=x_flat.device, dtype=x_flat.dtype)
+    ws_bytes = _native.workspace_size_k1_dw(T, nC, D_out)
+    ws = torch.empty(max(ws_bytes, 1), device=x_flat.device, dtype=torch.uint8)
+    _native.call("fmhc_k1_bwd_dw", grad_out.data_ptr(), x_flat.data_ptr(), inv_rms.data_ptr(),
+                 grad_W.data_ptr(), ws.data_ptr(), ws_bytes, T, nC, D_out, _stream(x_flat))
+    return grad_W
+
+
+@torch.library.impl(_lib, "fused_rmsnorm_project_backward", "CUDA")
+def _fused_rmsnorm_project_backward_cuda(grad_out, x_flat, W, proj_out, inv_rms):
+    grad_out = _bf16("grad_out", grad_out)
+    x_flat = _bf16("x_flat", x_flat)
+    W = _bf16("W", W)
+    proj_out = _bf16("proj_out", proj_out)
+    inv_rms = inv_rms.to(torch.float32).contiguous()
+    T, nC = x_flat.shape
+    D_out = W.shape[0]
+    grad_x = torch.empty_like(x_flat)
+    with _on_device(x_flat):
+        _native.call("fmhc_k1_bwd_dx", grad_out.data_ptr(), x_flat.data_ptr(), W.data_ptr(),
+                     proj_out.data_ptr(), inv_rms.data_ptr(), grad_x.data_ptr(), T, nC, D_out,
+                     _stream(x_flat))
+        grad_W = _k1_grad_w(grad_out, x_flat, inv_rms, D_out)
+    return grad_x, grad_W
+
+
+@torch.library.impl(_lib, "fused_pre_map", "CUDA")
+def _fused_pre_map_cuda(x_streams: torch.Tensor, h_pre: torch.Tensor):
+    T, n, C = x_streams.shape
+    _n4("fused_pre_map", n)
+    x_streams = _bf16("x_streams", x_streams)
+    h_pre = _coef(h_pre)
+    out = torch.empty((T, C), device=x_streams.device, dtype=x_streams.dtype)
+    with _on_device(x_streams):
+        _native.call("fmhc_k3_fwd", x_streams.data_ptr(), h_pre.data_ptr(), out.data_ptr(),
+                     T, n, C, _stream(x_streams))
+    return out
+
+
+@torch.library.impl(_lib, "fused_pre_map_backward", "CUDA")
+def _fused_pre_map_backward_cuda(grad_out, x_streams, h_pre):
+    T, n, C = x_streams.shape
+    _n4("fused_pre_map_backward", n)
+    grad_out = _bf16("grad_out", grad_out)
+    x_streams = _bf16("x_streams", x_streams)
+    h_pre = _coef(h_pre)
+    grad_x = torch.empty_like(x_streams)
+    grad_h_pre = torch.empty((T, n), device=x_streams.device, dtype=torch.float32)
+    with _on_device(x_streams):
+        _native.call("fmhc_k3_bwd", grad_out.data_ptr(), x_streams.data_ptr(), h_pre.data_ptr(),
+                     grad_x.data_ptr(), grad_h_pre.data_ptr(), T, n, C, _stream(x_streams))
+    return grad_x, grad_h_pre
+
+
+@torch.library.impl(_lib, "fused_post_res", "CUDA")
+def _fused_post_res_cuda(x_streams, layer_output, H_merged, h_post):
+    T, n, C = x_streams.shape
+    _n4("fused_post_res", n)
+    x_streams = _bf16("x_streams", x_streams)
+    layer_output = _bf16("layer_output", layer_output)
+    H_merged = _coef(H_merged)
+    h_post = _coef(h_post)
+    out = torch.empty_like(x_streams)
+    with _on_device(x_streams):
+        _native.call("fmhc_k4_fwd", x_streams.data_ptr(), layer_output.data_ptr(),
+                     H_merged.data_ptr(), h_post.data_ptr(), out.data_ptr(), T, n, C,
+                     _stream(x_streams))
+    return out
+
+
+@torch.library.impl(_lib, "fused_post_res_backward", "CUDA")
+def _fused_post_res_backward_cuda(grad_out, x_streams, layer_output, H_merged, h_post):
+    T, n, C = x_streams.shape
+    _n4("fused_post_res_backward", n)
+    grad_out = _bf16("grad_out", grad_out)
+    x_streams = _bf16("x_streams", x_streams)
+    layer_output = _bf16("layer_output", layer_output)
+    H_merged = _coef(H_merged)
+    h_post = _coef(h_post)
+    grad_x = torch.empty_like(x_streams)
+    grad_layer_output = torch.empty((T, C), device=x_streams.device, dtype=x_streams.dtype)
+    grad_H = torch.empty((T, n, n), device=x_streams.device, dtype=torch.float32)
+    grad_hp = torch.empty((T, n), device=x_streams.device, dtype=torch.float32)
+    with _on_device(x_streams):
+        _native.call("fmhc_k4_bwd", grad_out.data_ptr(), x_streams.data_ptr(),
+                     layer_output.data_ptr(), H_merged.data_ptr(), h_post.data_ptr(),
+                     grad_x.data_ptr(), grad_layer_output.data_ptr(), grad_H.data_ptr(),
+                     grad_hp.data_ptr(), T, n, C, _stream(x_streams))
+    return grad_x, grad_layer_output, grad_H, grad_hp
+
+
+# ---------------------------------------------------------------------------
+# Autograd (src/flash_mhc/ops.py:670-714): inputs and outputs are saved; K1's
+# grad w.r.t. inv_rms is ignored, as in the reference.
+# ---------------------------------------------------------------------------
+
+
+def _setup_save_inputs_outputs(ctx, inputs, output):
+    if isinstance(output, tuple):
+        ctx.save_for_backward(*inputs, *output)
+    else:
+        ctx.save_for_backward(*inputs, output)
+
+
+def _fused_rmsnorm_project_backward(ctx, grad_out, grad_inv_rms):
+    x_flat, W, proj_out, inv_rms = ctx.saved_tensors
+    need_x, need_w = ctx.needs_input_grad[0], ctx.needs_input_grad[1]
+    if need_w:
+        grad_x, grad_W = torch.ops.flash_mhc.fused_rmsnorm_project_backward(
+            grad_out, x_flat, W, proj_out, inv_rms)
+        return (grad_x if need_x else None), grad_W
+    grad_x = torch.ops.flash_mhc.fused_rmsnorm_project_bwd_dx(
+        grad_out, x_flat, W, proj_out, inv_rms)
+    return grad_x, None
+
+
+def _fused_pre_map_backward(ctx, grad_out):
+    x_streams, h_pre, _out = ctx.saved_tensors
+    return torch.ops.flash_mhc.fused_pre_map_backward(grad_out, x_streams, h_pre)
+
+
+def _fused_post_res_backward(ctx, grad_out):
+    x_streams, layer_output, H_merged, h_post, _out = ctx.saved_tensors
+    return torch.ops.flash_mhc.fused_post_res_backward(
+        grad_out, x_streams, layer_output, H_merged, h_post)
+
+
+torch.library.register_autograd(
+    "flash_mhc::fused_rmsnorm_project",
+    _fused_rmsnorm_project_backward,
+    setup_context=_setup_save_inputs_outputs,
+)
+torch.library.register_autograd(
+    "flash_mhc::fused_pre_map",
+    _fused_pre_map_backward,
+    setup_context=_setup_save_inputs_outputs,
+)
+torch.library.register_autograd(
+    "flash_mhc::fused_post_res",
+    _fused_post_res_backward,
+    setup_context=_setup_save_inputs_outputs,
+)

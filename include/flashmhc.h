@@ -1,0 +1,151 @@
+/*
+ * flashmhc.h -- C ABI of the B200 (sm_100a) mHC-lite hot-path kernels.
+ *
+ * libflashmhc_sm100.so exports exactly the functions declared here.  Every
+ * entry point:
+ *   - takes raw device pointers, element counts and a cudaStream_t passed as
+ *     `void *` (NULL = legacy default stream); no torch or C++ types;
+ *   - launches asynchronously on that stream and never synchronises;
+ *   - allocates no device memory (any scratch is passed in by the caller);
+ *   - returns an fmhc_status; on failure fmhc_last_error() describes it
+ *     (thread-local; valid until the next call on the same thread);
+ *   - accepts T == 0 (returns FMHC_OK without launching).
+ *
+ * Tensor layouts are dense row-major.  n (number of residual streams) must be
+ * 4.  "bf16" buffers hold IEEE bfloat16 values, "f32" buffers IEEE float32.
+ * Coefficient buffers (h_pre, h_post, H_merged, their gradients, inv_rms) must
+ * be 16-byte aligned; bf16 buffers must be at least 2-byte aligned (16-byte
+ * alignment and C % 8 == 0 select the 128-bit vector path).
+ *
+ * Each function replaces one launch of the reference's Triton kernels; the
+ * reference interface it stands in for is cited beside it (paths relative to
+ * the alint77/flash-mHC project root).
+ */
+#ifndef FLASHMHC_H
+#define FLASHMHC_H
+
+#include <stdint.h>
+
+#if defined(__GNUC__)
+#define FMHC_API __attribute__((visibility("default")))
+#else
+#define FMHC_API
+#endif
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum fmhc_status {
+  FMHC_OK = 0,
+  FMHC_ERR_INVALID_ARGUMENT = 1, /* null pointer, negative size, n != 4 ... */
+  FMHC_ERR_UNSUPPORTED = 2,      /* shape the kernels do not implement      */
+  FMHC_ERR_ALIGNMENT = 3,        /* a pointer violates the alignment rule   */
+  FMHC_ERR_LAUNCH = 4,           /* the CUDA launch itself failed           */
+  FMHC_ERR_CUDA = 5,             /* another CUDA runtime/driver call failed */
+  FMHC_ERR_WORKSPACE = 6         /* caller-provided workspace too small     */
+} fmhc_status;
+
+/* Human-readable description of the last failure on this thread ("" if none). */
+FMHC_API const char *fmhc_last_error(void);
+
+/* Library version string, e.g. "flashmhc-sm100 0.1.0". */
+FMHC_API const char *fmhc_version(void);
+
+/* ------------------------------------------------------------------------
+ * K1 forward: fused RMSNorm + thin projection.
+ *   inv_rms[t] = rsqrt(sum_k x[t,k]^2 / nC + 1e-6)                    (f32)
+ *   out[t,d]   = bf16( (sum_k x[t,k] * W[d,k]) * inv_rms[t] )   f32 accumulate
+ * x (T, nC) bf16, W (D, nC) bf16 -> out (T, D) bf16, inv_rms (T,) f32.  D <= 32.
+ * Replaces op flash_mhc::fused_rmsnorm_project (src/flash_mhc/ops.py:24-26,
+ * 205-264) and kernel _fused_rmsnorm_project_fwd_kernel
+ * (src/flash_mhc/kernels.py:250-303).
+ */
+FMHC_API int fmhc_k1_fwd(const void *x, const void *W, void *out, float *inv_rms,
+                int64_t T, int64_t nC, int64_t D, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K1 backward, grad_x only.
+ *   s[t]       = (sum_d go[t,d] * proj[t,d]) * inv_rms[t]^2 / nC
+ *   grad_x[t,k]= bf16( inv_rms[t] * sum_d go[t,d] W[d,k] - s[t] * x[t,k] )
+ * grad_out, proj (T, D) bf16; x (T, nC) bf16; W (D, nC) bf16; inv_rms (T,) f32
+ * -> grad_x (T, nC) bf16.
+ * Replaces op flash_mhc::fused_rmsnorm_project_bwd_dx (src/flash_mhc/ops.py:27-29,
+ * 267-344) and kernel _fused_rmsnorm_project_bwd_dx_kernel
+ * (src/flash_mhc/kernels.py:306-376).
+ */
+FMHC_API int fmhc_k1_bwd_dx(const void *grad_out, const void *x, const void *W,
+                   const void *proj, const float *inv_rms, void *grad_x,
+                   int64_t T, int64_t nC, int64_t D, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K1 weight gradient.
+ *   grad_W[d,k] = bf16( sum_t bf16(go[t,d] * inv_rms[t]) * x[t,k] )   f32 accumulate
+ * grad_out (T, D) bf16, x (T, nC) bf16, inv_rms (T,) f32 -> grad_W (D, nC) bf16.
+ * `workspace` is caller-owned device memory of at least
+ * fmhc_k1_bwd_dw_workspace_size(T, nC, D) bytes (256-byte aligned); its
+ * contents on entry do not matter.
+ * Replaces the cuBLAS matmul in the K1 autograd formula
+ * (src/flash_mhc/ops.py:683-684).
+ */
+FMHC_API int64_t fmhc_k1_bwd_dw_workspace_size(int64_t T, int64_t nC, int64_t D);
+FMHC_API int fmhc_k1_bwd_dw(const void *grad_out, const void *x, const float *inv_rms,
+                   void *grad_W, void *workspace, int64_t workspace_bytes,
+                   int64_t T, int64_t nC, int64_t D, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K3 forward: pre-map of the n streams into the layer input.
+ *   out[t,c] = bf16( sum_j h_pre[t,j] * x[t,j,c] )
+ * x (T, n, C) bf16, h_pre (T, n) f32 -> out (T, C) bf16.
+ * Replaces op flash_mhc::fused_pre_map (src/flash_mhc/ops.py:31, 347-414) and
+ * kernel _fused_pre_map_fwd_kernel (src/flash_mhc/kernels.py:673-717).
+ */
+FMHC_API int fmhc_k3_fwd(const void *x, const float *h_pre, void *out,
+                int64_t T, int64_t n, int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K3 backward (fused).
+ *   grad_x[t,j,c] = bf16( h_pre[t,j] * go[t,c] )
+ *   grad_h[t,j]   = sum_c x[t,j,c] * go[t,c]                         (f32)
+ * grad_out (T, C) bf16, x (T, n, C) bf16, h_pre (T, n) f32
+ * -> grad_x (T, n, C) bf16, grad_h (T, n) f32.
+ * Replaces op flash_mhc::fused_pre_map_backward (src/flash_mhc/ops.py:32-34,
+ * 417-493) and kernel _fused_pre_map_bwd_fused_kernel_n4
+ * (src/flash_mhc/kernels.py:720-853).
+ */
+FMHC_API int fmhc_k3_bwd(const void *grad_out, const void *x, const float *h_pre,
+                void *grad_x, float *grad_h,
+                int64_t T, int64_t n, int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K4 forward: post-res mixing.
+ *   out[t,i,c] = bf16( sum_j H[t,i,j] * x[t,j,c] + h_post[t,i] * lo[t,c] )
+ * x (T, n, C) bf16, lo (T, C) bf16, H (T, n, n) f32, h_post (T, n) f32
+ * -> out (T, n, C) bf16.
+ * Replaces op flash_mhc::fused_post_res (src/flash_mhc/ops.py:36-38, 496-567)
+ * and kernel _fused_post_res_fwd_kernel_n4 (src/flash_mhc/kernels.py:384-481).
+ */
+FMHC_API int fmhc_k4_fwd(const void *x, const void *lo, const float *H,
+                const float *h_post, void *out,
+                int64_t T, int64_t n, int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K4 backward (fused, one pass over grad_out, x and lo).
+ *   grad_lo[t,c]  = bf16( sum_i h_post[t,i] * go[t,i,c] )
+ *   grad_hp[t,i]  = sum_c go[t,i,c] * lo[t,c]                        (f32)
+ *   grad_H[t,i,j] = sum_c go[t,i,c] * x[t,j,c]                       (f32)
+ *   grad_x[t,j,c] = bf16( sum_i H[t,i,j] * go[t,i,c] )
+ * Replaces op flash_mhc::fused_post_res_backward (src/flash_mhc/ops.py:39-41,
+ * 570-667) and kernel _fused_post_res_bwd_fused_kernel_n4
+ * (src/flash_mhc/kernels.py:487-665).
+ */
+FMHC_API int fmhc_k4_bwd(const void *grad_out, const void *x, const void *lo,
+                const float *H, const float *h_post,
+                void *grad_x, void *grad_lo, float *grad_H, float *grad_hp,
+                int64_t T, int64_t n, int64_t C, void *stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* FLASHMHC_H */

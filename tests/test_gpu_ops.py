@@ -1,0 +1,235 @@
+"""GPU parity of the six kernels (+ the K1 weight gradient) against the CPU oracle.
+
+Every call goes through ``torch.ops.flash_mhc`` -> ctypes -> the C ABI of
+libflashmhc_sm100.so.  Inputs are seeded; the oracle (oracle/mhc_oracle.py,
+pinned to the reference in tests/test_oracle.py) computes in float64 on the
+same bf16 inputs.
+
+Tolerances (north star of this build):
+* bf16 outputs: |got - ref| <= 2e-2 + 1e-2 * |ref|;
+* f32 reductions (grad_h, grad_H, grad_h_post): |got - ref| <= 1e-4 * sum|terms|
+  (the scale of f32 accumulation error; terms cancel, so |ref| is not a bound);
+* inv_rms: relative 1e-5.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+from oracle import mhc_oracle as O
+from tests._util import assert_close, assert_sum_close, load_golden
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device"),
+]
+
+BF_ATOL, BF_RTOL = 2e-2, 1e-2
+RED_REL = 1e-4
+
+
+def _bf(a, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev).to(torch.bfloat16)
+
+
+def _f32(a, dev="cuda"):
+    return torch.from_numpy(np.ascontiguousarray(a, dtype=np.float32)).to(dev)
+
+
+def _np(t):
+    return t.detach().float().cpu().numpy()
+
+
+def _inputs(T, C, seed, outlier=False):
+    rng = np.random.default_rng(seed)
+    x = rng.standard_normal((T, 4, C)).astype(np.float32)
+    if outlier:
+        cols = rng.choice(C, size=max(1, C // 100), replace=False)
+        x[:, :, cols] *= 100.0
+    x = O.bf16_round(x)
+    lo = O.bf16_round(rng.standard_normal((T, C)))
+    W = O.bf16_round(rng.standard_normal((32, 4 * C)) * 0.02)
+    hp = rng.standard_normal((T, 4)).astype(np.float32)
+    hpost = rng.standard_normal((T, 4)).astype(np.float32)
+    H = rng.standard_normal((T, 4, 4)).astype(np.float32)
+    g_pre = O.bf16_round(rng.standard_normal((T, C)))
+    g_post = O.bf16_round(rng.standard_normal((T, 4, C)))
+    g_proj = O.bf16_round(rng.standard_normal((T, 32)))
+    return dict(x=x, lo=lo, W=W, hp=hp, hpost=hpost, H=H, g_pre=g_pre, g_post=g_post,
+                g_proj=g_proj)
+
+
+SHAPES = [
+    (2048, 256, False),   # the reference test size (tests/test_correctness.py:95, 163, 206)
+    (1, 64, False),       # tiny T
+    (16, 768, True),      # edge config C=768 with 1% x100 outlier channels
+    (257, 1024, False),   # T not a multiple of any tile
+    (40, 100, False),     # C % 8 != 0 -> 4-wide vector path
+    (33, 97, False),      # odd C -> scalar path
+]
+
+
+@pytest.mark.parametrize("T,C,outlier", SHAPES)
+def test_k3_fwd_bwd(T, C, outlier):
+    d = _inputs(T, C, 10 + T + C, outlier)
+    x, hp, go = _bf(d["x"]), _f32(d["hp"]), _bf(d["g_pre"])
+    out = torch.ops.flash_mhc.fused_pre_map(x, hp)
+    assert out.dtype == torch.bfloat16 and out.shape == (T, C)
+    assert_close("k3_fwd", _np(out), O.k3_fwd(d["x"], d["hp"]), BF_ATOL, BF_RTOL)
+    gx, gh = torch.ops.flash_mhc.fused_pre_map_backward(go, x, hp)
+    rgx, rgh = O.k3_bwd(d["g_pre"], d["x"], d["hp"])
+    assert_close("k3_gx", _np(gx), rgx, BF_ATOL, BF_RTOL)
+    assert gh.dtype == torch.float32
+    assert_sum_close("k3_gh", _np(gh), rgh, O.k3_bwd_abs(d["g_pre"], d["x"]), RED_REL)
+
+
+@pytest.mark.parametrize("T,C,outlier", SHAPES)
+def test_k4_fwd_bwd(T, C, outlier):
+    d = _inputs(T, C, 20 + T + C, outlier)
+    x, lo, H, hpost, go = _bf(d["x"]), _bf(d["lo"]), _f32(d["H"]), _f32(d["hpost"]), _bf(d["g_post"])
+    out = torch.ops.flash_mhc.fused_post_res(x, lo, H, hpost)
+    assert out.shape == (T, 4, C)
+    assert_close("k4_fwd", _np(out), O.k4_fwd(d["x"], d["lo"], d["H"], d["hpost"]), BF_ATOL,
+                 BF_RTOL)
+    gx, glo, gH, ghp = torch.ops.flash_mhc.fused_post_res_backward(go, x, lo, H, hpost)
+    rgx, rglo, rgH, rghp = O.k4_bwd(d["g_post"], d["x"], d["lo"], d["H"], d["hpost"])
+    sH, sP = O.k4_bwd_abs(d["g_post"], d["x"], d["lo"])
+    assert_close("k4_gx", _np(gx), rgx, BF_ATOL, BF_RTOL)
+    assert_close("k4_glo", _np(glo), rglo, BF_ATOL, BF_RTOL)
+    assert_sum_close("k4_gH", _np(gH), rgH, sH, RED_REL)
+    assert_sum_close("k4_ghp", _np(ghp), rghp, sP, RED_REL)
+
+
+def _check_gw(got, go, xf, inv):
+    ref = O.k1_bwd_dw(go, xf, inv)
+    gos = O.bf16_round(go.astype(np.float64) * inv.astype(np.float64)[:, None]).astype(np.float64)
+    scale = np.abs(gos).T @ np.abs(xf.astype(np.float64))
+    diff = np.abs(got.astype(np.float64) - ref)
+    lim = BF_RTOL * np.abs(ref) + RED_REL * scale + 1e-6
+    assert np.all(diff <= lim), f"k1_gW: worst {np.max(diff / lim):.3g} x bound"
+
+
+@pytest.mark.parametrize("T,C,outlier", SHAPES)
+def test_k1_fwd_bwd(T, C, outlier):
+    d = _inputs(T, C, 30 + T + C, outlier)
+    xf_np = d["x"].reshape(T, 4 * C)
+    xf, W, go = _bf(xf_np), _bf(d["W"]), _bf(d["g_proj"])
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
+    rout, rinv = O.k1_fwd(xf_np, d["W"])
+    assert out.dtype == torch.bfloat16 and inv.dtype == torch.float32
+    assert_close("k1_inv_rms", _np(inv), rinv, 0, 1e-5)
+    assert_close("k1_out", _np(out), rout, BF_ATOL, BF_RTOL)
+    # backward from the kernel's own proj/inv_rms (what autograd feeds it)
+    proj_np, inv_np = _np(out), _np(inv)
+    gx = torch.ops.flash_mhc.fused_rmsnorm_project_bwd_dx(go, xf, W, out, inv)
+    rgx = O.k1_bwd_dx(d["g_proj"], xf_np, d["W"], proj_np, inv_np)
+    assert_close("k1_gx", _np(gx), rgx, BF_ATOL, BF_RTOL)
+    gx2, gW = torch.ops.flash_mhc.fused_rmsnorm_project_backward(go, xf, W, out, inv)
+    assert torch.equal(gx, gx2)
+    _check_gw(_np(gW), d["g_proj"], xf_np, inv_np)
+
+
+def test_k1_autograd_contract():
+    """fused_rmsnorm_project's registered autograd returns (grad_x, grad_W)."""
+    d = _inputs(64, 64, 5)
+    xf_np = d["x"].reshape(64, 256)
+    xf = _bf(xf_np).requires_grad_(True)
+    W = _bf(d["W"]).requires_grad_(True)
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
+    go = _bf(d["g_proj"])
+    (out.float() * go.float()).sum().backward()
+    rgx = O.k1_bwd_dx(d["g_proj"], xf_np, d["W"], _np(out), _np(inv))
+    assert_close("grad_x", _np(xf.grad), rgx, BF_ATOL, BF_RTOL)
+    _check_gw(_np(W.grad), d["g_proj"], xf_np, _np(inv))
+
+
+def test_golden_inputs_through_cuda_ops():
+    """The reference-generated fixture inputs, through the CUDA ops, against the
+    oracle (tight) and against the reference restatements (the reference
+    test's own tolerances, tests/test_correctness.py:48-51)."""
+    g = load_golden("ops_bf16")
+    T = int(g["T"])
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(_bf(g["k1_x"]), _bf(g["k1_W"]))
+    assert_close("k1 vs oracle", _np(out), O.k1_fwd(g["k1_x"], g["k1_W"])[0], BF_ATOL, BF_RTOL)
+    assert_close("k1 vs reference", _np(out), g["k1_out"], 1e-2, 1.6e-2)
+    out = torch.ops.flash_mhc.fused_pre_map(_bf(g["k3_x"]), _f32(g["k3_h"]))
+    assert_close("k3 vs reference", _np(out), g["k3_out"], 1e-2, 1.6e-2)
+    gx, gh = torch.ops.flash_mhc.fused_pre_map_backward(_bf(g["k3_go"]), _bf(g["k3_x"]),
+                                                        _f32(g["k3_h"]))
+    assert_close("k3 gx vs reference", _np(gx), g["k3_gx"], 5e-2, 2e-2)
+    assert_close("k3 gh vs reference", _np(gh), g["k3_gh"], 5e-2, 2e-2)
+    out = torch.ops.flash_mhc.fused_post_res(_bf(g["k4_x"]), _bf(g["k4_lo"]), _f32(g["k4_H"]),
+                                             _f32(g["k4_hp"]))
+    assert_close("k4 vs reference", _np(out), g["k4_out"], 1e-2, 1.6e-2)
+    r = torch.ops.flash_mhc.fused_post_res_backward(_bf(g["k4_go"]), _bf(g["k4_x"]),
+                                                    _bf(g["k4_lo"]), _f32(g["k4_H"]),
+                                                    _f32(g["k4_hp"]))
+    for got, k in zip(r, ("k4_gx", "k4_glo", "k4_gH", "k4_ghp")):
+        assert_close(k + " vs reference", _np(got), g[k], 5e-2, 2e-2)
+    assert T == 64
+
+
+def test_zero_tokens():
+    x = torch.empty(0, 4, 64, device="cuda", dtype=torch.bfloat16)
+    assert torch.ops.flash_mhc.fused_pre_map(x, torch.empty(0, 4, device="cuda")).shape == (0, 64)
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(
+        x.reshape(0, 256), torch.zeros(32, 256, device="cuda", dtype=torch.bfloat16))
+    assert out.shape == (0, 32) and inv.shape == (0,)
+
+
+def test_non_contiguous_inputs_are_handled():
+    """The reference assumes contiguity silently; here inputs are made contiguous."""
+    d = _inputs(64, 128, 3)
+    x = _bf(d["x"])
+    xt = x.transpose(0, 1).contiguous().transpose(0, 1)  # same values, non-contiguous
+    assert not xt.is_contiguous()
+    hp = _f32(d["hp"])
+    assert torch.equal(torch.ops.flash_mhc.fused_pre_map(xt, hp),
+                       torch.ops.flash_mhc.fused_pre_map(x, hp))
+
+
+def test_n_not_4_raises_value_error():
+    x = torch.zeros(8, 3, 64, device="cuda", dtype=torch.bfloat16)
+    with pytest.raises(ValueError):
+        torch.ops.flash_mhc.fused_pre_map(x, torch.zeros(8, 3, device="cuda"))
+
+
+def test_full_size_against_torch_fp32():
+    """Metric shape T=65536, C=1024: the kernels against a torch float32
+    restatement on the GPU (the CPU oracle would take minutes at this size)."""
+    torch.manual_seed(0)
+    T, C = 65536, 1024
+    x = torch.randn(T, 4, C, device="cuda").bfloat16()
+    lo = torch.randn(T, C, device="cuda").bfloat16()
+    H = torch.randn(T, 4, 4, device="cuda")
+    hp = torch.randn(T, 4, device="cuda")
+    go = torch.randn(T, 4, C, device="cuda").bfloat16()
+    xf32, lof, gof = x.float(), lo.float(), go.float()
+    out = torch.ops.flash_mhc.fused_post_res(x, lo, H, hp)
+    ref = torch.einsum("tij,tjc->tic", H, xf32) + hp[:, :, None] * lof[:, None, :]
+    torch.testing.assert_close(out.float(), ref, atol=BF_ATOL, rtol=BF_RTOL)
+    del out, ref
+    gx, glo, gH, ghp = torch.ops.flash_mhc.fused_post_res_backward(go, x, lo, H, hp)
+    torch.testing.assert_close(glo.float(), torch.einsum("ti,tic->tc", hp, gof), atol=BF_ATOL,
+                               rtol=BF_RTOL)
+    torch.testing.assert_close(gx.float(), torch.einsum("tij,tic->tjc", H, gof), atol=BF_ATOL,
+                               rtol=BF_RTOL)
+    sH = torch.einsum("tic,tjc->tij", gof.abs(), xf32.abs())
+    dH = (gH - torch.einsum("tic,tjc->tij", gof, xf32)).abs()
+    assert bool((dH <= RED_REL * sH).all())
+    dP = (ghp - torch.einsum("tic,tc->ti", gof, lof)).abs()
+    assert bool((dP <= RED_REL * torch.einsum("tic,tc->ti", gof.abs(), lof.abs())).all())
+    del gx, glo, gH, ghp
+    h = torch.randn(T, 4, device="cuda")
+    out = torch.ops.flash_mhc.fused_pre_map(x, h)
+    torch.testing.assert_close(out.float(), torch.einsum("tj,tjc->tc", h, xf32), atol=BF_ATOL,
+                               rtol=BF_RTOL)
+    W = (torch.randn(32, 4 * C, device="cuda") * 0.02).bfloat16()
+    xf = x.reshape(T, 4 * C)
+    proj, inv = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
+    rinv = torch.rsqrt((xf.float() ** 2).mean(1) + 1e-6)
+    torch.testing.assert_close(inv, rinv, atol=0, rtol=1e-5)
+    rproj = (xf.float() @ W.float().t()) * rinv[:, None]
+    torch.testing.assert_close(proj.float(), rproj, atol=BF_ATOL, rtol=BF_RTOL)
