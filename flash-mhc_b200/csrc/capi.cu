@@ -67,6 +67,16 @@ const char *fmhc_last_error(void) { return g_err; }
 
 const char *fmhc_version(void) { return "flashmhc-sm100 0.1.0"; }
 
+int fmhc_check_device_error(int *code) {
+  if (code == nullptr) return fail(FMHC_ERR_INVALID_ARGUMENT, "fmhc_check_device_error: code is NULL");
+  if (cudaDeviceSynchronize() != cudaSuccess)
+    return fail(FMHC_ERR_CUDA, "fmhc_check_device_error: %s", cudaGetErrorString(cudaGetLastError()));
+  unsigned v = 0;
+  if (fmhc::read_device_error(&v)) return fail(FMHC_ERR_CUDA, "fmhc_check_device_error: symbol copy failed");
+  *code = int(v);
+  return ok();
+}
+
 int fmhc_k3_fwd(const void *x, const float *h_pre, void *out, int64_t T, int64_t n, int64_t C,
                 void *stream) {
   const char *w = "fmhc_k3_fwd";

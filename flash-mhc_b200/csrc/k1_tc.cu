@@ -1,15 +1,358 @@
-// K1 forward on the tensor cores: placeholder until the tcgen05 kernel lands.
+// K1 forward on the 5th-generation tensor cores.
+//
+//   inv_rms[t] = rsqrt(sum_k x[t,k]^2 / nC + 1e-6)
+//   out[t,d]   = bf16( (sum_k x[t,k] W[d,k]) * inv_rms[t] )        (D = 32)
+//
+// (src/flash_mhc/kernels.py:250-303 of the reference.)  At ~32 FLOP/byte the
+// projection needs ~210 TFLOP/s to keep up with HBM, beyond the CUDA cores, so
+// the (T, nC) x (nC, 32) contraction runs as tcgen05.mma with the accumulator
+// in TMEM while the sum of squares is taken by CUDA cores from the same
+// shared-memory tiles.
+//
+// Persistent kernel, one CTA per SM, 6 warps:
+//   warp 0     TMA producer: x tile (<=128 rows x 64 k, four 32-row boxes,
+//              128-byte swizzle) + W chunk (32 x 64) per pipeline stage;
+//   warp 1     MMA issuer: 4 x tcgen05.mma M128 N32 K16 per stage into one of
+//              two TMEM accumulators (64 columns allocated);
+//   warps 2-5  one thread per tile row: sum of squares from shared memory,
+//              then the epilogue (tcgen05.ld of the row's 32 f32 columns,
+//              scale by inv_rms, bf16 store).
+// Each CTA owns a contiguous token range in 32-row units (balanced to within
+// 32 rows across CTAs); partial tiles load only the 32-row boxes they need.
+// Every mbarrier wait is bounded (sm100_ptx.cuh): on expiry the kernel records
+// an error code, drains its copies and MMAs (bounded), frees TMEM and returns.
+#include <cuda.h>
+#include <cudaTypedefs.h>
+
+#include <cstdio>
+
+#include "fmhc_common.cuh"
 #include "k1_tc.h"
+#include "sm100_ptx.cuh"
 
 namespace fmhc {
+namespace k1tc {
 
-bool k1_tc_fwd_supported(const void *, const void *, const void *, const float *, int64_t,
-                         int64_t, int64_t) {
-  return false;
+using namespace sm100;
+
+constexpr int kBM = 128;            // tile rows (MMA M)
+constexpr int kBK = 64;             // k per stage: one 128-byte swizzled row
+constexpr int kND = 32;             // projection width (MMA N)
+constexpr int kBoxRows = 32;        // TMA box rows for x
+constexpr int kStages = 8;
+constexpr int kABytes = kBM * kBK * 2;        // 16 KiB
+constexpr int kBBytes = kND * kBK * 2;        // 4 KiB
+constexpr int kBoxBytes = kBoxRows * kBK * 2; // 4 KiB
+constexpr int kStageBytes = kABytes + kBBytes;
+constexpr int kThreads = 192;
+constexpr uint32_t kTmemCols = 64;  // two 32-column accumulators
+constexpr float kEps = 1e-6f;
+
+struct alignas(1024) FwdSmem {
+  uint8_t stage[kStages][kStageBytes];  // 20 KiB each, 1 KiB aligned
+  uint64_t full[kStages];
+  uint64_t empty[kStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+// Error sites recorded in g_device_error.
+enum : unsigned { kSiteProdEmpty = 0x101, kSiteMmaFull = 0x102, kSiteMmaTempty = 0x103,
+                  kSiteEpiFull = 0x104, kSiteEpiTfull = 0x105, kSiteDrain = 0x106 };
+
+__global__ void __launch_bounds__(kThreads, 1)
+k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                 const __grid_constant__ CUtensorMap tmap_w, __nv_bfloat16 *__restrict__ out,
+                 float *__restrict__ inv_rms, int64_t T, int nC, int64_t units) {
+  extern __shared__ uint8_t smem_raw[];
+  FwdSmem &sm = *reinterpret_cast<FwdSmem *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int *abort = &sm.abort;
+
+  // Contiguous token range of this CTA, in 32-row units.
+  const int64_t u0 = int64_t(blockIdx.x) * units / gridDim.x;
+  const int64_t u1 = int64_t(blockIdx.x + 1) * units / gridDim.x;
+  const int64_t t_begin = u0 * kBoxRows;
+  const int64_t t_end = (u1 * kBoxRows < T) ? u1 * kBoxRows : T;
+  const int ntiles = t_end > t_begin ? int((t_end - t_begin + kBM - 1) / kBM) : 0;
+  const int nk = nC / kBK;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kStages; ++s) {
+      mbar_init(smem_u32(&sm.full[s]), 1);
+      mbar_init(smem_u32(&sm.empty[s]), 1 + 4);  // MMA commit + 4 row warps
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sm.tfull[b]), 1);
+      mbar_init(smem_u32(&sm.tempty[b]), 4);
+    }
+    mbar_init(smem_u32(&sm.mma_done), 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), kTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      int issued = 0;
+      for (int tile = 0; tile < ntiles && !*abort; ++tile) {
+        const int64_t row0 = t_begin + int64_t(tile) * kBM;
+        const int64_t rows = (t_end - row0) < kBM ? (t_end - row0) : kBM;
+        const int nbox = int((rows + kBoxRows - 1) / kBoxRows);
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, abort, kSiteProdEmpty)) break;
+          const uint32_t full = smem_u32(&sm.full[stage]);
+          mbar_arrive_expect_tx(full, uint32_t(nbox * kBoxBytes + kBBytes));
+          const uint32_t a = smem_u32(sm.stage[stage]);
+          for (int b = 0; b < nbox; ++b)
+            tma_load_2d(a + b * kBoxBytes, &tmap_x, full, kb * kBK, int32_t(row0 + b * kBoxRows));
+          tma_load_2d(a + kABytes, &tmap_w, full, kb * kBK, 0);
+          ++issued;
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+      }
+      // Drain: the last min(issued, kStages) loads must have landed before exit.
+      int n = issued < kStages ? issued : kStages;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < n; ++i) {
+        if (--s < 0) { s = kStages - 1; ph ^= 1; }
+        mbar_wait(smem_u32(&sm.full[s]), ph, abort, kSiteDrain, true);
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, kND, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      int acc = 0;
+      uint32_t acc_phase = 0;
+      for (int tile = 0; tile < ntiles && !*abort; ++tile) {
+        if (!mbar_wait(smem_u32(&sm.tempty[acc]), acc_phase ^ 1, abort, kSiteMmaTempty)) break;
+        tc_fence_after();
+        const uint32_t d = tmem + uint32_t(acc * kND);
+        bool ok = true;
+        for (int kb = 0; kb < nk; ++kb) {
+          if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteMmaFull)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a = smem_u32(sm.stage[stage]);
+#pragma unroll
+          for (int k = 0; k < kBK / 16; ++k) {
+            const uint64_t ad = smem_desc(a + k * 32, 16, 1024, 2);
+            const uint64_t bd = smem_desc(a + kABytes + k * 32, 16, 1024, 2);
+            mma_bf16_ss(d, ad, bd, idesc, (kb | k) != 0);
+          }
+          mma_commit(smem_u32(&sm.empty[stage]));
+          if (++stage == kStages) { stage = 0; phase ^= 1; }
+        }
+        if (!ok) break;
+        mma_commit(smem_u32(&sm.tfull[acc]));
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      }
+      // All MMAs issued by this thread complete before TMEM is freed.
+      mma_commit(smem_u32(&sm.mma_done));
+      mbar_wait(smem_u32(&sm.mma_done), 0, abort, kSiteDrain, true);
+    }
+  } else {
+    // ------------------------------------------ row warps: sumsq + epilogue
+    const int q = warp & 3;  // TMEM lane quarter this warp may access
+    const int r = q * 32 + lane;
+    int stage = 0;
+    uint32_t phase = 0;
+    int acc = 0;
+    uint32_t acc_phase = 0;
+    for (int tile = 0; tile < ntiles && !*abort; ++tile) {
+      const int64_t row0 = t_begin + int64_t(tile) * kBM;
+      const int64_t rows = (t_end - row0) < kBM ? (t_end - row0) : kBM;
+      float ss = 0.f;
+      bool ok = true;
+      for (int kb = 0; kb < nk; ++kb) {
+        if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteEpiFull)) { ok = false; break; }
+        const uint8_t *row = sm.stage[stage] + r * 128;
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          // Any order covers the row; rotating by r keeps the 8 rows of a
+          // swizzle atom on distinct banks.
+          const uint4 u = *reinterpret_cast<const uint4 *>(row + (((i + r) & 7) << 4));
+          float f;
+          f = bf16lo(u.x); ss = fmaf(f, f, ss); f = bf16hi(u.x); ss = fmaf(f, f, ss);
+          f = bf16lo(u.y); ss = fmaf(f, f, ss); f = bf16hi(u.y); ss = fmaf(f, f, ss);
+          f = bf16lo(u.z); ss = fmaf(f, f, ss); f = bf16hi(u.z); ss = fmaf(f, f, ss);
+          f = bf16lo(u.w); ss = fmaf(f, f, ss); f = bf16hi(u.w); ss = fmaf(f, f, ss);
+        }
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.empty[stage]));
+        if (++stage == kStages) { stage = 0; phase ^= 1; }
+      }
+      if (!ok) break;
+      if (!mbar_wait(smem_u32(&sm.tfull[acc]), acc_phase, abort, kSiteEpiTfull)) break;
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * kND), v);
+      tmem_wait_ld();
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.tempty[acc]));
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      if (r < rows) {
+        const int64_t t = row0 + r;
+        const float inv = rsqrtf(ss / float(nC) + kEps);
+        uint4 *o = reinterpret_cast<uint4 *>(out + t * kND);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 w;
+          w.x = pack_bf16x2(__uint_as_float(v[8 * c + 0]) * inv, __uint_as_float(v[8 * c + 1]) * inv);
+          w.y = pack_bf16x2(__uint_as_float(v[8 * c + 2]) * inv, __uint_as_float(v[8 * c + 3]) * inv);
+          w.z = pack_bf16x2(__uint_as_float(v[8 * c + 4]) * inv, __uint_as_float(v[8 * c + 5]) * inv);
+          w.w = pack_bf16x2(__uint_as_float(v[8 * c + 6]) * inv, __uint_as_float(v[8 * c + 7]) * inv);
+          __stcs(o + c, w);
+        }
+        __stcs(inv_rms + t, inv);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kTmemCols);
+  }
 }
-int launch_k1_tc_fwd(const void *, const void *, void *, float *, int64_t, int, cudaStream_t) {
-  return 2;
+
+// ------------------------------------------------------------------- host side
+namespace {
+
+thread_local char g_msg[256] = "";
+
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  static bool tried = false;
+  if (!tried) {
+    tried = true;
+    void *p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) ==
+            cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
+  }
+  return fn;
 }
-const char *k1_tc_error() { return "tensor-core K1 not built"; }
+
+// 2-D bf16 tensor map: inner dimension `inner` (contiguous), `outer` rows of
+// `row_bytes` stride, box inner x outer_box, 128-byte swizzle, zero fill.
+bool make_map(CUtensorMap *m, const void *base, uint64_t inner, uint64_t outer,
+              uint64_t row_bytes, uint32_t box_inner, uint32_t box_outer,
+              CUtensorMapSwizzle swz) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t dims[2] = {inner, outer};
+  cuuint64_t strides[1] = {row_bytes};
+  cuuint32_t box[2] = {box_inner, box_outer};
+  cuuint32_t estr[2] = {1, 1};
+  CUresult r = fn(m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, const_cast<void *>(base), dims, strides,
+                  box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+int device_sms() {
+  int dev = 0, sms = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+  return sms;
+}
+
+// Opt in to the kernel's dynamic shared memory once per (kernel, device).
+int set_smem_attr(const void *kernel, size_t bytes) {
+  static thread_local const void *done_kernel[8][16] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 16) dev = 15;
+  for (int i = 0; i < 8; ++i) {
+    if (done_kernel[i][dev] == kernel) return 0;
+    if (done_kernel[i][dev] == nullptr) {
+      if (cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) !=
+          cudaSuccess) {
+        snprintf(g_msg, sizeof(g_msg), "cudaFuncSetAttribute(smem=%zu) failed", bytes);
+        return 5;
+      }
+      done_kernel[i][dev] = kernel;
+      return 0;
+    }
+  }
+  return cudaFuncSetAttribute(kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, int(bytes)) ==
+                 cudaSuccess ? 0 : 5;
+}
+
+bool device_is_sm100() {
+  int dev = 0, major = 0, minor = 0;
+  cudaGetDevice(&dev);
+  cudaDeviceGetAttribute(&major, cudaDevAttrComputeCapabilityMajor, dev);
+  cudaDeviceGetAttribute(&minor, cudaDevAttrComputeCapabilityMinor, dev);
+  return major == 10 && minor == 0;
+}
+
+}  // namespace
+}  // namespace k1tc
+
+const char *k1_tc_error() { return k1tc::g_msg; }
+
+bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
+                         int64_t T, int64_t nC, int64_t D) {
+  if (D != k1tc::kND || nC % k1tc::kBK != 0 || T < 1 || T > (int64_t(1) << 31)) return false;
+  if ((reinterpret_cast<uintptr_t>(x) | reinterpret_cast<uintptr_t>(W)) & 15) return false;
+  if ((reinterpret_cast<uintptr_t>(out) & 15) || (reinterpret_cast<uintptr_t>(inv_rms) & 3))
+    return false;
+  return k1tc::device_is_sm100() && k1tc::encode_fn() != nullptr;
+}
+
+int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t T, int nC,
+                     cudaStream_t s) {
+  using namespace k1tc;
+  CUtensorMap mx, mw;
+  if (!make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, kBK, kBoxRows,
+                CU_TENSOR_MAP_SWIZZLE_128B) ||
+      !make_map(&mw, W, uint64_t(nC), kND, uint64_t(nC) * 2, kBK, kND,
+                CU_TENSOR_MAP_SWIZZLE_128B)) {
+    snprintf(g_msg, sizeof(g_msg), "cuTensorMapEncodeTiled failed");
+    return 5;
+  }
+  const int64_t units = (T + kBoxRows - 1) / kBoxRows;
+  int64_t grid = device_sms();
+  if (grid > units) grid = units;
+  const size_t smem = sizeof(FwdSmem) + 1024;
+  if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_kernel), smem)) return e;
+  k1_fwd_tc_kernel<<<unsigned(grid), kThreads, smem, s>>>(
+      mx, mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units);
+  return 0;
+}
+
+int read_device_error(unsigned *code) {
+  unsigned v = 0, zero = 0;
+  if (cudaMemcpyFromSymbol(&v, sm100::g_device_error, sizeof(v)) != cudaSuccess) return 5;
+  if (v && cudaMemcpyToSymbol(sm100::g_device_error, &zero, sizeof(zero)) != cudaSuccess) return 5;
+  *code = v;
+  return 0;
+}
 
 }  // namespace fmhc

@@ -15,4 +15,7 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
                      cudaStream_t s);
 const char *k1_tc_error();
 
+// Reads and clears the per-device error word set by expired bounded waits.
+int read_device_error(unsigned *code);
+
 }  // namespace fmhc

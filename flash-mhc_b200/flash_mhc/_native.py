@@ -26,6 +26,7 @@ _i64 = ctypes.c_int64
 _SIGNATURES = {
     "fmhc_last_error": [],
     "fmhc_version": [],
+    "fmhc_check_device_error": [ctypes.POINTER(ctypes.c_int)],
     "fmhc_k1_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k1_bwd_dx": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k1_bwd_dw_workspace_size": [_i64, _i64, _i64],
@@ -98,6 +99,13 @@ def call(name: str, *args) -> None:
 
 def workspace_size_k1_dw(T: int, nC: int, D: int) -> int:
     return int(lib().fmhc_k1_bwd_dw_workspace_size(T, nC, D))
+
+
+def check_device_error() -> int:
+    """Synchronise the current device and return (and clear) its device error word."""
+    code = ctypes.c_int(0)
+    call("fmhc_check_device_error", ctypes.byref(code))
+    return code.value
 
 
 def version() -> str:

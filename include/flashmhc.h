@@ -52,6 +52,15 @@ FMHC_API const char *fmhc_last_error(void);
 /* Library version string, e.g. "flashmhc-sm100 0.1.0". */
 FMHC_API const char *fmhc_version(void);
 
+/* Failure detection for the tensor-core kernels.  Every wait of those kernels
+ * on a barrier is bounded (about 1 s); a wait that expires makes the kernel
+ * record a non-zero site code in a per-device error word, release its
+ * resources and return early (its outputs are then invalid).  This call
+ * synchronises the current device, stores the word in *code (0 = no expired
+ * wait since the last call) and clears it.  No reference counterpart: the
+ * reference's Triton kernels have no device-side failure reporting. */
+FMHC_API int fmhc_check_device_error(int *code);
+
 /* ------------------------------------------------------------------------
  * K1 forward: fused RMSNorm + thin projection.
  *   inv_rms[t] = rsqrt(sum_k x[t,k]^2 / nC + 1e-6)                    (f32)

@@ -78,8 +78,9 @@ def test_block_matches_float64_oracle():
     x = torch.from_numpy(g["x"]).cuda().to(torch.bfloat16).requires_grad_(True)
     out = blk(x)
     (out.float() * torch.from_numpy(g["g"]).cuda()).sum().backward()
-    params = dict(alpha_pre=float(blk.alpha_pre.float()), alpha_post=float(blk.alpha_post.float()),
-                  alpha_res=float(blk.alpha_res.float()),
+    params = dict(alpha_pre=float(blk.alpha_pre.detach().float()),
+                  alpha_post=float(blk.alpha_post.detach().float()),
+                  alpha_res=float(blk.alpha_res.detach().float()),
                   W=blk.W_all.weight.detach().float().cpu().numpy(),
                   bias=blk.W_all.bias.detach().float().cpu().numpy(), perm=g["perm"],
                   Wl=blk.layer.proj.weight.detach().float().cpu().numpy())
@@ -149,8 +150,10 @@ def test_eval_no_grad_tiny_T_with_outliers(T):
     assert out.shape == (T, 4, C)
     torch.testing.assert_close(out.float(), ref.float(), atol=5e-2, rtol=2e-2)
     params = dict(alpha_pre=0.01, alpha_post=0.01, alpha_res=0.01,
-                  W=blk.W_all.weight.float().cpu().numpy(), bias=blk.W_all.bias.float().cpu().numpy(),
-                  perm=blk.perm_mat.float().cpu().numpy(), Wl=blk.layer.weight.float().cpu().numpy())
+                  W=blk.W_all.weight.detach().float().cpu().numpy(),
+                  bias=blk.W_all.bias.detach().float().cpu().numpy(),
+                  perm=blk.perm_mat.float().cpu().numpy(),
+                  Wl=blk.layer.weight.detach().float().cpu().numpy())
     r = O.block_forward_backward(params, xb.float().cpu().numpy(), np.zeros((T, 4, C)),
                                  rms_eps=1e-6, layer="linear")
-    assert_close("out vs oracle", out.float().cpu().numpy(), r["out"], 2e-2 * 100, 1e-2)
+    assert_close("out vs oracle", out.float().cpu().numpy(), r["out"], 5e-2, 2e-2)

@@ -233,3 +233,40 @@ def test_full_size_against_torch_fp32():
     torch.testing.assert_close(inv, rinv, atol=0, rtol=1e-5)
     rproj = (xf.float() @ W.float().t()) * rinv[:, None]
     torch.testing.assert_close(proj.float(), rproj, atol=BF_ATOL, rtol=BF_RTOL)
+
+
+def _kernel_names(fn):
+    from torch.profiler import ProfilerActivity, profile
+
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
+
+
+def test_metric_shape_runs_the_tensor_core_k1():
+    """At T=65536, nC=4096 the K1 forward is the TMA + tcgen05 kernel."""
+    d = _inputs(256, 1024, 9)
+    xf = torch.randn(65536, 4096, device="cuda").bfloat16()
+    W = _bf(np.tile(d["W"], (1, 1)))
+    names = _kernel_names(lambda: torch.ops.flash_mhc.fused_rmsnorm_project(xf, W))
+    assert any("k1_fwd_tc_kernel" in n for n in names), names
+
+
+@pytest.mark.parametrize("T", [1, 31, 33, 1000, 4733])
+def test_k1_fwd_token_partitioning(T):
+    """Token ranges split across CTAs in 32-row units, partial tiles and boxes."""
+    C = 256
+    d = _inputs(T, C, 40 + T)
+    xf_np = d["x"].reshape(T, 4 * C)
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(_bf(xf_np), _bf(d["W"]))
+    rout, rinv = O.k1_fwd(xf_np, d["W"])
+    assert_close("inv_rms", _np(inv), rinv, 0, 1e-5)
+    assert_close("out", _np(out), rout, BF_ATOL, BF_RTOL)
+
+
+def test_no_device_error_recorded():
+    """No bounded wait of the tensor-core kernels expired during this module."""
+    from flash_mhc import _native
+
+    assert _native.check_device_error() == 0
