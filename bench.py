@@ -38,7 +38,6 @@ import argparse
 import json
 import os
 import statistics
-import subprocess
 import sys
 import time
 from pathlib import Path
@@ -94,58 +93,74 @@ def dram_traffic() -> dict:
 # ---------------------------------------------------------------------------
 
 class ClockSampler:
-    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    """Samples SM clock and throttle reasons of the given GPUs during a region.
 
-    def __init__(self, gpu_indices):
-        self.idx = gpu_indices
-        self.proc = None
-        self.path = Path("/tmp") / f"fmhc_clocks_{os.getpid()}.csv"
+    Polls NVML (read-only queries) from a background thread every few ms, so
+    even a timed region of a few tens of ms gets samples.
+    """
+
+    REASONS = {  # NVML clocks-event reason bits
+        "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40,
+        "hw_power_brake_slowdown": 0x80, "sw_power_cap": 0x4,
+    }
+
+    def __init__(self, gpu_indices, period_s=0.005):
+        self.idx = list(gpu_indices)
+        self.period = period_s
+        self.samples = []  # (sm_mhz, max_mhz, reasons_bitmask)
+        self._stop = None
+        self._thread = None
+        self.err = None
 
     def __enter__(self):
         if not self.idx:
             return self
+        import threading
+
         try:
-            self.fh = open(self.path, "w")
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-i", ",".join(str(i) for i in self.idx), "-lms", "200"],
-                stdout=self.fh, stderr=subprocess.DEVNULL)
-        except Exception:
-            self.proc = None
+            import pynvml
+
+            pynvml.nvmlInit()
+            handles = [pynvml.nvmlDeviceGetHandleByIndex(i) for i in self.idx]
+            maxes = [pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM) for h in handles]
+        except Exception as e:  # pragma: no cover - depends on the box
+            self.err = f"nvml unavailable: {e}"
+            return self
+        self._stop = threading.Event()
+
+        def loop():
+            while not self._stop.is_set():
+                for h, mx in zip(handles, maxes):
+                    try:
+                        sm = pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM)
+                        rs = pynvml.nvmlDeviceGetCurrentClocksEventReasons(h)
+                        self.samples.append((sm, mx, rs))
+                    except Exception as e:  # pragma: no cover
+                        self.err = str(e)
+                self._stop.wait(self.period)
+
+        self._thread = threading.Thread(target=loop, daemon=True)
+        self._thread.start()
         return self
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except Exception:
-                self.proc.kill()
-            self.fh.close()
+        if self._thread is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self) -> dict:
-        if self.proc is None or not self.path.exists():
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["nvidia-smi unavailable"]}
-        sm, smax, reasons = [], [], set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for line in self.path.read_text().splitlines():
-            f = [x.strip() for x in line.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                smax.append(float(f[2]))
-            except ValueError:
-                continue
-            for name, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": None,
+                    "reasons": [self.err or "no samples"]}
+        sm = [s[0] for s in self.samples]
+        reasons = set()
+        for _, _, rs in self.samples:
+            for name, bit in self.REASONS.items():
+                if rs & bit:
                     reasons.add(name)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["no samples"]}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(smax),
-                "samples": len(sm), "reasons": sorted(reasons)}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(s[1] for s in self.samples),
+                "sm_min_mhz": min(sm), "samples": len(sm), "source": "nvml",
+                "reasons": sorted(reasons)}
 
 
 # ---------------------------------------------------------------------------

@@ -178,39 +178,61 @@ int fmhc_k1_bwd_dx(const void *grad_out, const void *x, const void *W, const voi
   FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, W);
   FMHC_REQUIRE_ALIGN2(w, proj); FMHC_REQUIRE_ALIGN2(w, grad_x);
   if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
-  const int vec = pick_vec(nC, {x, W, grad_x});
-  fmhc::launch_k1_bwd_dx_simt(grad_out, x, W, proj, inv_rms, grad_x, T, int(nC), int(D),
-                              vec == 8 ? 8 : 1, (cudaStream_t)stream);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (fmhc::k1_tc_bwd_supported(grad_out, x, W, proj, grad_x, T, nC, D)) {
+    if (int e = fmhc::launch_k1_tc_bwd(grad_out, x, W, proj, inv_rms, grad_x, nullptr, nullptr, 0,
+                                       T, int(nC), s))
+      return fail(e, "%s: %s", w, fmhc::k1_tc_error());
+  } else {
+    const int vec = pick_vec(nC, {x, W, grad_x});
+    fmhc::launch_k1_bwd_dx_simt(grad_out, x, W, proj, inv_rms, grad_x, T, int(nC), int(D),
+                                vec == 8 ? 8 : 1, s);
+  }
   return check_launch(w);
 }
 
-int64_t fmhc_k1_bwd_dw_workspace_size(int64_t T, int64_t nC, int64_t D) {
-  if (T <= 0 || nC <= 0 || D <= 0) return 0;
-  return fmhc::k1_dw_workspace_bytes(T, nC, D);
+int64_t fmhc_k1_bwd_workspace_size(int64_t T, int64_t nC, int64_t D) {
+  if (T <= 0 || nC <= 0 || D <= 0 || D > 32) return 0;
+  const int64_t a = fmhc::k1_tc_bwd_workspace_bytes(T, nC);
+  const int64_t b = fmhc::k1_dw_workspace_bytes(T, nC, D);
+  return a > b ? a : b;
 }
 
-int fmhc_k1_bwd_dw(const void *grad_out, const void *x, const float *inv_rms, void *grad_W,
-                   void *workspace, int64_t workspace_bytes, int64_t T, int64_t nC, int64_t D,
-                   void *stream) {
-  const char *w = "fmhc_k1_bwd_dw";
+int fmhc_k1_bwd(const void *grad_out, const void *x, const void *W, const void *proj,
+                const float *inv_rms, void *grad_x, void *grad_W, void *workspace,
+                int64_t workspace_bytes, int64_t T, int64_t nC, int64_t D, void *stream) {
+  const char *w = "fmhc_k1_bwd";
   if (int e = check_k1(w, T, nC, D)) return e;
   FMHC_REQUIRE_PTR(w, grad_W);
   cudaStream_t s = (cudaStream_t)stream;
   if (T == 0) {
-    // Empty batch: the gradient is exactly zero.
+    // Empty batch: the weight gradient is exactly zero.
     if (cudaMemsetAsync(grad_W, 0, size_t(D * nC) * 2, s) != cudaSuccess)
       return fail(FMHC_ERR_CUDA, "%s: cudaMemsetAsync failed", w);
     return ok();
   }
-  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, inv_rms);
+  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, W);
+  FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, inv_rms); FMHC_REQUIRE_PTR(w, grad_x);
   FMHC_REQUIRE_PTR(w, workspace);
-  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, grad_W);
+  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, W);
+  FMHC_REQUIRE_ALIGN2(w, proj); FMHC_REQUIRE_ALIGN2(w, grad_x); FMHC_REQUIRE_ALIGN2(w, grad_W);
+  if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
   if (!aligned(workspace, 256)) return fail(FMHC_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", w);
-  const int64_t need = fmhc::k1_dw_workspace_bytes(T, nC, D);
+  const int64_t need = fmhc_k1_bwd_workspace_size(T, nC, D);
   if (workspace_bytes < need)
     return fail(FMHC_ERR_WORKSPACE, "%s: workspace of %lld bytes, %lld needed", w,
                 (long long)workspace_bytes, (long long)need);
-  fmhc::launch_k1_dw_simt(grad_out, x, inv_rms, grad_W, (float *)workspace, T, int(nC), int(D), s);
+  if (fmhc::k1_tc_bwd_supported(grad_out, x, W, proj, grad_x, T, nC, D)) {
+    if (int e = fmhc::launch_k1_tc_bwd(grad_out, x, W, proj, inv_rms, grad_x, grad_W, workspace,
+                                       workspace_bytes, T, int(nC), s))
+      return fail(e, "%s: %s", w, fmhc::k1_tc_error());
+  } else {
+    const int vec = pick_vec(nC, {x, W, grad_x});
+    fmhc::launch_k1_bwd_dx_simt(grad_out, x, W, proj, inv_rms, grad_x, T, int(nC), int(D),
+                                vec == 8 ? 8 : 1, s);
+    fmhc::launch_k1_dw_simt(grad_out, x, inv_rms, grad_W, (float *)workspace, T, int(nC),
+                            int(D), s);
+  }
   return check_launch(w);
 }
 

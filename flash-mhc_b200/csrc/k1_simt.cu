@@ -178,7 +178,7 @@ __global__ void k1_dw_reduce_kernel(const float *__restrict__ ws, bf16 *__restri
 int k1_dw_splits(int64_t T) {
   int64_t s = (T + 1023) / 1024;
   if (s < 1) s = 1;
-  if (s > 64) s = 64;
+  if (s > 16) s = 16;
   return int(s);
 }
 

@@ -238,6 +238,14 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
+}  // namespace k1tc
+}  // namespace fmhc
+
+#include "k1_tc_bwd.cuh"
+
+namespace fmhc {
+namespace k1tc {
+
 // ------------------------------------------------------------------- host side
 namespace {
 
@@ -317,6 +325,9 @@ bool device_is_sm100() {
 
 const char *k1_tc_error() { return k1tc::g_msg; }
 
+static_assert(sizeof(k1tc::BwdSmem) + 1024 <= 232448, "K1 backward shared memory");
+static_assert(sizeof(k1tc::FwdSmem) + 1024 <= 232448, "K1 forward shared memory");
+
 bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
                          int64_t T, int64_t nC, int64_t D) {
   if (D != k1tc::kND || nC % k1tc::kBK != 0 || T < 1 || T > (int64_t(1) << 31)) return false;
@@ -344,6 +355,117 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
   if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_kernel), smem)) return e;
   k1_fwd_tc_kernel<<<unsigned(grid), kThreads, smem, s>>>(
       mx, mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units);
+  return 0;
+}
+
+// ---------------------------------------------------------------- K1 backward
+namespace k1tc {
+namespace {
+
+struct BwdPlan {
+  int ntt, nkc, grid, maxseg;
+  int64_t units;
+  int64_t gos_bytes, part_bytes;
+};
+
+int64_t round256(int64_t b) { return (b + 255) & ~int64_t(255); }
+
+BwdPlan bwd_plan(int64_t T, int64_t nC) {
+  BwdPlan p{};
+  p.ntt = int((T + kBwdBT - 1) / kBwdBT);
+  p.nkc = int(nC / kBwdBK);
+  p.units = int64_t(p.nkc) * p.ntt;
+  int64_t g = device_sms();
+  if (g > p.units) g = p.units;
+  if (g < 1) g = 1;
+  p.grid = int(g);
+  p.maxseg = 1;
+  for (int c = 0; c < p.grid; ++c) {
+    const int64_t c0 = int64_t(c) * p.units / p.grid, c1 = int64_t(c + 1) * p.units / p.grid;
+    if (c1 <= c0) continue;
+    const int segs = int((c1 - 1) / p.ntt - c0 / p.ntt + 1);
+    if (segs > p.maxseg) p.maxseg = segs;
+  }
+  p.gos_bytes = round256(T * kND * 2);
+  p.part_bytes = round256(int64_t(p.grid) * p.maxseg * kND * kBwdBK * 4);
+  return p;
+}
+
+}  // namespace
+}  // namespace k1tc
+
+bool k1_tc_bwd_supported(const void *go, const void *x, const void *W, const void *proj,
+                         const void *gx, int64_t T, int64_t nC, int64_t D) {
+  if (D != k1tc::kND || nC % k1tc::kBwdBK != 0 || T < 1 || T > (int64_t(1) << 31)) return false;
+  const uintptr_t m = reinterpret_cast<uintptr_t>(go) | reinterpret_cast<uintptr_t>(x) |
+                      reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(proj) |
+                      reinterpret_cast<uintptr_t>(gx);
+  if (m & 15) return false;
+  return k1tc::device_is_sm100() && k1tc::encode_fn() != nullptr;
+}
+
+int64_t k1_tc_bwd_workspace_bytes(int64_t T, int64_t nC) {
+  if (T < 1 || nC % k1tc::kBwdBK) return 0;
+  const k1tc::BwdPlan p = k1tc::bwd_plan(T, nC);
+  return p.gos_bytes + p.part_bytes;
+}
+
+int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *proj,
+                     const float *inv_rms, void *gx, void *gW, void *ws, int64_t ws_bytes,
+                     int64_t T, int nC, cudaStream_t s) {
+  using namespace k1tc;
+  const BwdPlan p = bwd_plan(T, nC);
+  const bool with_dw = gW != nullptr;
+  uint8_t *gos = nullptr;
+  float *part = nullptr;
+  if (with_dw) {
+    if (ws == nullptr || ws_bytes < p.gos_bytes + p.part_bytes ||
+        (reinterpret_cast<uintptr_t>(ws) & 255)) {
+      snprintf(g_msg, sizeof(g_msg), "workspace of %lld bytes (need %lld, 256-byte aligned)",
+               (long long)ws_bytes, (long long)(p.gos_bytes + p.part_bytes));
+      return 6;
+    }
+    gos = static_cast<uint8_t *>(ws);
+    part = reinterpret_cast<float *>(gos + p.gos_bytes);
+  }
+  CUtensorMap mx, mgx, mgo, mgos, mw;
+  bool ok = make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBwdBT,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map(&mgx, gx, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBwdBT,
+                     CU_TENSOR_MAP_SWIZZLE_128B) &&
+            make_map(&mgo, go, kND, uint64_t(T), kND * 2, kND, kBwdBT, CU_TENSOR_MAP_SWIZZLE_64B) &&
+            make_map(&mgos, with_dw ? gos : go, kND, uint64_t(T), kND * 2, kND, kBwdBT,
+                     CU_TENSOR_MAP_SWIZZLE_64B) &&
+            make_map(&mw, W, uint64_t(nC), kND, uint64_t(nC) * 2, 64, kND,
+                     CU_TENSOR_MAP_SWIZZLE_128B);
+  if (!ok) {
+    snprintf(g_msg, sizeof(g_msg), "cuTensorMapEncodeTiled failed");
+    return 5;
+  }
+  if (with_dw) {
+    const int64_t n8 = T * (kND / 8);
+    k1_bwd_gos_kernel<<<unsigned((n8 + 255) / 256), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(go), inv_rms, reinterpret_cast<__nv_bfloat16 *>(gos), T);
+  }
+  const size_t smem = sizeof(BwdSmem) + 1024;
+  if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_bwd_tc_kernel), smem)) return e;
+  BwdArgs args;
+  args.go = static_cast<const __nv_bfloat16 *>(go);
+  args.proj = static_cast<const __nv_bfloat16 *>(proj);
+  args.inv_rms = inv_rms;
+  args.dw_part = part;
+  args.T = T;
+  args.nC = nC;
+  args.ntt = p.ntt;
+  args.units = p.units;
+  args.maxseg = p.maxseg;
+  args.with_dw = with_dw ? 1 : 0;
+  k1_bwd_tc_kernel<<<unsigned(p.grid), kThreads, smem, s>>>(mx, mgx, mgo, mgos, mw, args);
+  if (with_dw) {
+    const int64_t n = int64_t(kND) * nC;
+    k1_bwd_dw_reduce_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(
+        part, static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.units, p.grid, p.maxseg);
+  }
   return 0;
 }
 

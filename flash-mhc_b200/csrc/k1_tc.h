@@ -15,6 +15,15 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
                      cudaStream_t s);
 const char *k1_tc_error();
 
+// Backward (grad_x, and grad_W when gW != nullptr) on the tensor cores.
+bool k1_tc_bwd_supported(const void *go, const void *x, const void *W, const void *proj,
+                         const void *gx, int64_t T, int64_t nC, int64_t D);
+// Caller workspace for the grad_W variant on the current device (0 if unsupported shape).
+int64_t k1_tc_bwd_workspace_bytes(int64_t T, int64_t nC);
+int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *proj,
+                     const float *inv_rms, void *gx, void *gW, void *ws, int64_t ws_bytes,
+                     int64_t T, int nC, cudaStream_t s);
+
 // Reads and clears the per-device error word set by expired bounded waits.
 int read_device_error(unsigned *code);
 

@@ -1,0 +1,382 @@
+// K1 backward on the tensor cores: grad_x and (optionally) grad_W in one pass
+// over x.  Included by k1_tc.cu (same translation unit as the forward kernel,
+// sharing its PTX helpers and device error word).
+//
+//   s[t]        = (sum_d go[t,d] proj[t,d]) * inv_rms[t]^2 / nC
+//   grad_x[t,k] = bf16( inv_rms[t] * sum_d go[t,d] W[d,k] - s[t] * x[t,k] )
+//   grad_W[d,k] = bf16( sum_t gos[t,d] x[t,k] ),  gos = bf16(go * inv_rms)
+//
+// (src/flash_mhc/kernels.py:306-376 and src/flash_mhc/ops.py:683-684 of the
+// reference.)  Work unit = (k-chunk of 128 columns, tile of 128 tokens); the
+// units are ordered k-chunk-major and each persistent CTA takes a contiguous
+// run of them, so it sweeps token tiles for one k-chunk at a time:
+//
+//   warp 0     TMA producer: per unit x[128 t x 128 k] (two 64-column boxes,
+//              128-byte swizzle), go[128 t x 32] and gos[128 t x 32] (64-byte
+//              swizzle); per k-chunk segment the W chunk [32 x 128 k].
+//   warp 1     MMA issuer, per unit:
+//                grad_W: D2[k, d] += x^T (MN-major A) * gos (MN-major B),
+//                        8 x M128 N32 K16, accumulated over the segment;
+//                grad_x: D1[t, k]  = go (K-major A) * W^T (MN-major B),
+//                        2 x M128 N128 K16 into one of two TMEM buffers.
+//   warps 2-5  one thread per token row: grad_x = inv*D1 - s*x written over x
+//              in the stage buffer, then stored by TMA; at a segment end the
+//              grad_W partial D2 (thread per k row) goes to the workspace.
+// A second small kernel reduces the per-CTA grad_W partials in a fixed order
+// (deterministic) and rounds to bf16.
+#pragma once
+
+namespace fmhc {
+namespace k1tc {
+
+constexpr int kBwdBT = 128;                       // tokens per unit (MMA M of grad_x)
+constexpr int kBwdBK = 128;                       // k per unit (MMA N of grad_x, M of grad_W)
+constexpr int kBwdStages = 4;
+constexpr int kBwdXBytes = kBwdBT * kBwdBK * 2;   // 32 KiB (two 16 KiB boxes)
+constexpr int kBwdXBox = kBwdBT * 64 * 2;         // 16 KiB
+constexpr int kBwdGBytes = kBwdBT * kND * 2;      // 8 KiB  (go or gos tile)
+constexpr int kBwdStageBytes = kBwdXBytes + 2 * kBwdGBytes;  // 48 KiB
+constexpr int kBwdWBytes = kND * kBwdBK * 2;      // 8 KiB  (two 4 KiB boxes)
+constexpr uint32_t kBwdTmemCols = 512;            // 2 x 128 (grad_x) + 32 (grad_W)
+constexpr uint32_t kBwdDwCol = 256;
+
+struct alignas(1024) BwdSmem {
+  uint8_t stage[kBwdStages][kBwdStageBytes];
+  uint8_t wbuf[2][kBwdWBytes];
+  uint64_t full[kBwdStages];
+  uint64_t empty[kBwdStages];
+  uint64_t tfull[2];
+  uint64_t tempty[2];
+  uint64_t wfull[2];
+  uint64_t wempty[2];
+  uint64_t dwfull;
+  uint64_t dwempty;
+  uint64_t epi;       // the 4 epilogue warps finished writing grad_x of a unit
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+enum : unsigned { kSiteBProdEmpty = 0x201, kSiteBProdW = 0x202, kSiteBMmaFull = 0x203,
+                  kSiteBMmaTempty = 0x204, kSiteBMmaW = 0x205, kSiteBMmaDw = 0x206,
+                  kSiteBEpiFull = 0x207, kSiteBEpiTfull = 0x208, kSiteBEpiDw = 0x209,
+                  kSiteBDrain = 0x20a, kSiteBEpiStore = 0x20b };
+
+struct BwdArgs {
+  const __nv_bfloat16 *go;    // (T, 32)
+  const __nv_bfloat16 *proj;  // (T, 32)
+  const float *inv_rms;       // (T,)
+  float *dw_part;             // [grid][maxseg][32][128] f32 (only with_dw)
+  int64_t T;
+  int nC;
+  int ntt;                    // token tiles
+  int64_t units;              // (nC / 128) * ntt
+  int maxseg;
+  int with_dw;
+};
+
+// Unit u -> (k-chunk, token tile).
+__device__ __forceinline__ void bwd_unit(int64_t u, int ntt, int &kc, int &tt) {
+  kc = int(u / ntt);
+  tt = int(u - int64_t(kc) * ntt);
+}
+
+__global__ void __launch_bounds__(kThreads, 1)
+k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                 const __grid_constant__ CUtensorMap tmap_gx,
+                 const __grid_constant__ CUtensorMap tmap_go,
+                 const __grid_constant__ CUtensorMap tmap_gos,
+                 const __grid_constant__ CUtensorMap tmap_w, const BwdArgs a) {
+  extern __shared__ uint8_t smem_raw[];
+  BwdSmem &sm = *reinterpret_cast<BwdSmem *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int *abort = &sm.abort;
+
+  const int64_t u0 = int64_t(blockIdx.x) * a.units / gridDim.x;
+  const int64_t u1 = int64_t(blockIdx.x + 1) * a.units / gridDim.x;
+
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < kBwdStages; ++s) {
+      mbar_init(smem_u32(&sm.full[s]), 1);
+      mbar_init(smem_u32(&sm.empty[s]), 1);  // released by the epilogue after its store read
+    }
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(smem_u32(&sm.tfull[b]), 1);
+      mbar_init(smem_u32(&sm.tempty[b]), 4);
+      mbar_init(smem_u32(&sm.wfull[b]), 1);
+      mbar_init(smem_u32(&sm.wempty[b]), 1);
+    }
+    mbar_init(smem_u32(&sm.dwfull), 1);
+    mbar_init(smem_u32(&sm.dwempty), 4);
+    mbar_init(smem_u32(&sm.epi), 4);
+    mbar_init(smem_u32(&sm.mma_done), 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_gx);
+    prefetch_tmap(&tmap_go);
+    prefetch_tmap(&tmap_gos);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), kBwdTmemCols);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = sm.tmem_base;
+
+  if (warp == 0) {
+    // ------------------------------------------------------------ producer
+    if (lane == 0) {
+      int stage = 0, issued = 0, seg = -1, kc_prev = -1;
+      uint32_t phase = 0;
+      const uint32_t tx = uint32_t(kBwdXBytes + (a.with_dw ? 2 : 1) * kBwdGBytes);
+      for (int64_t u = u0; u < u1 && !*abort; ++u) {
+        int kc, tt;
+        bwd_unit(u, a.ntt, kc, tt);
+        if (kc != kc_prev) {  // new segment: W chunk into wbuf[seg & 1]
+          ++seg;
+          kc_prev = kc;
+          const int wb = seg & 1;
+          if (!mbar_wait(smem_u32(&sm.wempty[wb]), ((seg >> 1) & 1) ^ 1, abort, kSiteBProdW)) break;
+          const uint32_t wf = smem_u32(&sm.wfull[wb]);
+          mbar_arrive_expect_tx(wf, kBwdWBytes);
+          tma_load_2d(smem_u32(sm.wbuf[wb]), &tmap_w, wf, kc * kBwdBK, 0);
+          tma_load_2d(smem_u32(sm.wbuf[wb]) + kBwdWBytes / 2, &tmap_w, wf, kc * kBwdBK + 64, 0);
+        }
+        if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, abort, kSiteBProdEmpty)) break;
+        const uint32_t f = smem_u32(&sm.full[stage]);
+        const uint32_t base = smem_u32(sm.stage[stage]);
+        const int32_t row0 = tt * kBwdBT;
+        mbar_arrive_expect_tx(f, tx);
+        tma_load_2d(base, &tmap_x, f, kc * kBwdBK, row0);
+        tma_load_2d(base + kBwdXBox, &tmap_x, f, kc * kBwdBK + 64, row0);
+        tma_load_2d(base + kBwdXBytes, &tmap_go, f, 0, row0);
+        if (a.with_dw) tma_load_2d(base + kBwdXBytes + kBwdGBytes, &tmap_gos, f, 0, row0);
+        ++issued;
+        if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
+      }
+      const int n = issued < kBwdStages ? issued : kBwdStages;
+      int s = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < n; ++i) {
+        if (--s < 0) { s = kBwdStages - 1; ph ^= 1; }
+        mbar_wait(smem_u32(&sm.full[s]), ph, abort, kSiteBDrain, true);
+      }
+    }
+  } else if (warp == 1) {
+    // ---------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc_dx = idesc_bf16_f32(kBwdBT, kBwdBK, 0, 1);
+      constexpr uint32_t idesc_dw = idesc_bf16_f32(kBwdBK, kND, 1, 1);
+      int stage = 0, acc = 0, seg = -1, kc_prev = -1;
+      uint32_t phase = 0, acc_phase = 0;
+      bool first_in_seg = false;
+      for (int64_t u = u0; u < u1 && !*abort; ++u) {
+        int kc, tt;
+        bwd_unit(u, a.ntt, kc, tt);
+        if (kc != kc_prev) {
+          ++seg;
+          kc_prev = kc;
+          first_in_seg = true;
+          if (a.with_dw && seg > 0 &&
+              !mbar_wait(smem_u32(&sm.dwempty), (seg - 1) & 1, abort, kSiteBMmaDw))
+            break;
+          if (!mbar_wait(smem_u32(&sm.wfull[seg & 1]), (seg >> 1) & 1, abort, kSiteBMmaW)) break;
+        }
+        int kc_next = -1, tt_next;
+        if (u + 1 < u1) bwd_unit(u + 1, a.ntt, kc_next, tt_next);
+        const bool last_in_seg = kc_next != kc;
+        if (!mbar_wait(smem_u32(&sm.tempty[acc]), acc_phase ^ 1, abort, kSiteBMmaTempty)) break;
+        if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteBMmaFull)) break;
+        tc_fence_after();
+        const uint32_t base = smem_u32(sm.stage[stage]);
+        if (a.with_dw) {
+          // grad_W: M = k (two 64-wide MN blocks 16 KiB apart), N = d, K = tokens.
+#pragma unroll
+          for (int k = 0; k < kBwdBT / 16; ++k) {
+            const uint64_t ad = smem_desc(base + k * 2048, kBwdXBox, 1024, 2);
+            const uint64_t bd = smem_desc(base + kBwdXBytes + kBwdGBytes + k * 1024, 512, 512, 4);
+            mma_bf16_ss(tmem + kBwdDwCol, ad, bd, idesc_dw, (first_in_seg && k == 0) ? 0u : 1u);
+          }
+        }
+        {
+          // grad_x: M = tokens, N = 128 k (two 64-wide MN blocks 4 KiB apart), K = d.
+          const uint32_t wb = smem_u32(sm.wbuf[seg & 1]);
+#pragma unroll
+          for (int k = 0; k < kND / 16; ++k) {
+            const uint64_t ad = smem_desc(base + kBwdXBytes + k * 32, 16, 512, 4);
+            const uint64_t bd = smem_desc(wb + k * 2048, kBwdWBytes / 2, 1024, 2);
+            mma_bf16_ss(tmem + uint32_t(acc * kBwdBK), ad, bd, idesc_dx, k != 0);
+          }
+        }
+        mma_commit(smem_u32(&sm.tfull[acc]));
+        if (last_in_seg) {
+          if (a.with_dw) mma_commit(smem_u32(&sm.dwfull));
+          mma_commit(smem_u32(&sm.wempty[seg & 1]));
+        }
+        first_in_seg = false;
+        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
+      }
+      mma_commit(smem_u32(&sm.mma_done));
+      mbar_wait(smem_u32(&sm.mma_done), 0, abort, kSiteBDrain, true);
+    }
+  } else {
+    // ------------------------------------------------------------ epilogue
+    const int q = warp & 3;
+    const int r = q * 32 + lane;  // token row of the unit / k row of the grad_W partial
+    const bool leader = (warp == 2 && lane == 0);
+    int stage = 0, acc = 0, seg = -1, kc_prev = -1, prev_stage = -1;
+    uint32_t phase = 0, acc_phase = 0, epi_phase = 0;
+    for (int64_t u = u0; u < u1 && !*abort; ++u) {
+      int kc, tt;
+      bwd_unit(u, a.ntt, kc, tt);
+      if (kc != kc_prev) { ++seg; kc_prev = kc; }
+      int kc_next = -1, tt_next;
+      if (u + 1 < u1) bwd_unit(u + 1, a.ntt, kc_next, tt_next);
+      const bool last_in_seg = kc_next != kc;
+
+      const int64_t t = int64_t(tt) * kBwdBT + r;
+      float s = 0.f, inv = 0.f;
+      if (t < a.T) {
+        // s = (go . proj) * inv^2 / nC from the stored forward output.
+        inv = a.inv_rms[t];
+        const uint4 *g4 = reinterpret_cast<const uint4 *>(a.go + t * kND);
+        const uint4 *p4 = reinterpret_cast<const uint4 *>(a.proj + t * kND);
+        float dot = 0.f;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const uint4 g = __ldg(g4 + c), p = __ldg(p4 + c);
+          dot = fmaf(bf16lo(g.x), bf16lo(p.x), dot); dot = fmaf(bf16hi(g.x), bf16hi(p.x), dot);
+          dot = fmaf(bf16lo(g.y), bf16lo(p.y), dot); dot = fmaf(bf16hi(g.y), bf16hi(p.y), dot);
+          dot = fmaf(bf16lo(g.z), bf16lo(p.z), dot); dot = fmaf(bf16hi(g.z), bf16hi(p.z), dot);
+          dot = fmaf(bf16lo(g.w), bf16lo(p.w), dot); dot = fmaf(bf16hi(g.w), bf16hi(p.w), dot);
+        }
+        s = dot * (inv * inv) / float(a.nC);
+      }
+      if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteBEpiFull)) break;
+      if (!mbar_wait(smem_u32(&sm.tfull[acc]), acc_phase, abort, kSiteBEpiTfull)) break;
+      tc_fence_after();
+      uint8_t *xs = sm.stage[stage];
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * kBwdBK + 32 * j), v);
+        tmem_wait_ld();
+        uint8_t *rowp = xs + (j >> 1) * kBwdXBox + r * 128;
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int chunk = ((j & 1) * 4 + c) ^ (r & 7);
+          uint4 *p = reinterpret_cast<uint4 *>(rowp + chunk * 16);
+          const uint4 xv = *p;
+          const float *dv = reinterpret_cast<const float *>(v + 8 * c);
+          uint4 o;
+          o.x = pack_bf16x2(fmaf(-s, bf16lo(xv.x), inv * dv[0]), fmaf(-s, bf16hi(xv.x), inv * dv[1]));
+          o.y = pack_bf16x2(fmaf(-s, bf16lo(xv.y), inv * dv[2]), fmaf(-s, bf16hi(xv.y), inv * dv[3]));
+          o.z = pack_bf16x2(fmaf(-s, bf16lo(xv.z), inv * dv[4]), fmaf(-s, bf16hi(xv.z), inv * dv[5]));
+          o.w = pack_bf16x2(fmaf(-s, bf16lo(xv.w), inv * dv[6]), fmaf(-s, bf16hi(xv.w), inv * dv[7]));
+          *p = o;
+        }
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.tempty[acc]));
+      // Every writer makes its grad_x visible to the TMA (async proxy), then
+      // one arrive per warp; only the store-issuing thread waits (bounded).
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.epi));
+      if (leader) {
+        if (!mbar_wait(smem_u32(&sm.epi), epi_phase, abort, kSiteBEpiStore)) break;
+        const uint32_t base = smem_u32(xs);
+        tma_store_2d(&tmap_gx, base, kc * kBwdBK, tt * kBwdBT);
+        tma_store_2d(&tmap_gx, base + kBwdXBox, kc * kBwdBK + 64, tt * kBwdBT);
+        tma_store_commit();
+        // The previous unit's store has finished reading its stage: release it.
+        tma_store_wait_read<1>();
+        if (prev_stage >= 0) mbar_arrive(smem_u32(&sm.empty[prev_stage]));
+        prev_stage = stage;
+      }
+      epi_phase ^= 1;
+      if (a.with_dw && last_in_seg) {
+        // grad_W partial of this segment: thread r owns k row r, 32 d columns.
+        if (!mbar_wait(smem_u32(&sm.dwfull), seg & 1, abort, kSiteBEpiDw)) break;
+        tc_fence_after();
+        uint32_t v[32];
+        tmem_ld_32x32b_x32(tmem + (uint32_t(q * 32) << 16) + kBwdDwCol, v);
+        tmem_wait_ld();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(smem_u32(&sm.dwempty));
+        const int sidx = seg < a.maxseg ? seg : a.maxseg - 1;
+        float *dst = a.dw_part + (int64_t(blockIdx.x) * a.maxseg + sidx) * (kND * kBwdBK) + r;
+#pragma unroll
+        for (int d = 0; d < kND; ++d) __stcg(dst + d * kBwdBK, __uint_as_float(v[d]));
+      }
+      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
+    }
+    if (leader) {
+      tma_store_wait_all<0>();
+      if (prev_stage >= 0) mbar_arrive(smem_u32(&sm.empty[prev_stage]));
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, kBwdTmemCols);
+  }
+}
+
+// gos[t, d] = bf16(go[t, d] * inv_rms[t]): the grad_W operand, rounded like
+// the reference's (grad_out * inv_rms).to(x.dtype).  One thread per 8 values.
+__global__ void k1_bwd_gos_kernel(const __nv_bfloat16 *__restrict__ go,
+                                  const float *__restrict__ inv_rms,
+                                  __nv_bfloat16 *__restrict__ gos, int64_t T) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // chunk of 8
+  if (i >= T * (kND / 8)) return;
+  const int64_t t = i / (kND / 8);
+  const float r = inv_rms[t];
+  const uint4 g = __ldg(reinterpret_cast<const uint4 *>(go) + i);
+  uint4 o;
+  o.x = pack_bf16x2(bf16lo(g.x) * r, bf16hi(g.x) * r);
+  o.y = pack_bf16x2(bf16lo(g.y) * r, bf16hi(g.y) * r);
+  o.z = pack_bf16x2(bf16lo(g.z) * r, bf16hi(g.z) * r);
+  o.w = pack_bf16x2(bf16lo(g.w) * r, bf16hi(g.w) * r);
+  reinterpret_cast<uint4 *>(gos)[i] = o;
+}
+
+// grad_W[d, k] = bf16(sum of the partials of every CTA whose unit range
+// touches k-chunk k / 128), in increasing CTA order.
+__global__ void k1_bwd_dw_reduce_kernel(const float *__restrict__ part,
+                                        __nv_bfloat16 *__restrict__ gW, int nC, int ntt,
+                                        int64_t units, int grid, int maxseg) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (i >= int64_t(kND) * nC) return;
+  const int d = int(i / nC);
+  const int k = int(i - int64_t(d) * nC);
+  const int kc = k / kBwdBK, kl = k - kc * kBwdBK;
+  const int64_t lo = int64_t(kc) * ntt, hi = lo + ntt;  // units of this k-chunk
+  int c = int(lo * grid / units) - 1;
+  if (c < 0) c = 0;
+  float acc = 0.f;
+  for (; c < grid; ++c) {
+    const int64_t c0 = int64_t(c) * units / grid, c1 = int64_t(c + 1) * units / grid;
+    if (c0 >= hi) break;
+    if (c1 <= lo || c1 <= c0) continue;
+    const int seg = kc - int(c0 / ntt);
+    if (seg < 0 || seg >= maxseg) continue;
+    acc += part[(int64_t(c) * maxseg + seg) * (kND * kBwdBK) + d * kBwdBK + kl];
+  }
+  gW[int64_t(d) * nC + k] = __float2bfloat16_rn(acc);
+}
+
+}  // namespace k1tc
+}  // namespace fmhc

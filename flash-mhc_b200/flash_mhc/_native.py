@@ -29,8 +29,8 @@ _SIGNATURES = {
     "fmhc_check_device_error": [ctypes.POINTER(ctypes.c_int)],
     "fmhc_k1_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k1_bwd_dx": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
-    "fmhc_k1_bwd_dw_workspace_size": [_i64, _i64, _i64],
-    "fmhc_k1_bwd_dw": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "fmhc_k1_bwd_workspace_size": [_i64, _i64, _i64],
+    "fmhc_k1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
     "fmhc_k3_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k3_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k4_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
@@ -39,7 +39,7 @@ _SIGNATURES = {
 _RESTYPES = {
     "fmhc_last_error": ctypes.c_char_p,
     "fmhc_version": ctypes.c_char_p,
-    "fmhc_k1_bwd_dw_workspace_size": _i64,
+    "fmhc_k1_bwd_workspace_size": _i64,
 }
 
 STATUS = {
@@ -97,8 +97,9 @@ def call(name: str, *args) -> None:
         raise FlashMHCError(name, st, msg)
 
 
-def workspace_size_k1_dw(T: int, nC: int, D: int) -> int:
-    return int(lib().fmhc_k1_bwd_dw_workspace_size(T, nC, D))
+def workspace_size_k1_bwd(T: int, nC: int, D: int) -> int:
+    """Bytes of scratch fmhc_k1_bwd needs on the current device."""
+    return int(lib().fmhc_k1_bwd_workspace_size(T, nC, D))
 
 
 def check_device_error() -> int:

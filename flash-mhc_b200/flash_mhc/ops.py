@@ -208,16 +208,6 @@ def _fused_rmsnorm_project_bwd_dx_cuda(grad_out, x_flat, W, proj_out, inv_rms):
     return grad_x
 
 
-def _k1_grad_w(grad_out, x_flat, inv_rms, D_out):
-    T, nC = x_flat.shape
-    grad_W = torch.empty((D_out, nC), device=x_flat.device, dtype=x_flat.dtype)
-    ws_bytes = _native.workspace_size_k1_dw(T, nC, D_out)
-    ws = torch.empty(max(ws_bytes, 1), device=x_flat.device, dtype=torch.uint8)
-    _native.call("fmhc_k1_bwd_dw", grad_out.data_ptr(), x_flat.data_ptr(), inv_rms.data_ptr(),
-                 grad_W.data_ptr(), ws.data_ptr(), ws_bytes, T, nC, D_out, _stream(x_flat))
-    return grad_W
-
-
 @torch.library.impl(_lib, "fused_rmsnorm_project_backward", "CUDA")
 def _fused_rmsnorm_project_backward_cuda(grad_out, x_flat, W, proj_out, inv_rms):
     grad_out = _bf16("grad_out", grad_out)
@@ -228,11 +218,13 @@ def _fused_rmsnorm_project_backward_cuda(grad_out, x_flat, W, proj_out, inv_rms)
     T, nC = x_flat.shape
     D_out = W.shape[0]
     grad_x = torch.empty_like(x_flat)
+    grad_W = torch.empty((D_out, nC), device=x_flat.device, dtype=x_flat.dtype)
     with _on_device(x_flat):
-        _native.call("fmhc_k1_bwd_dx", grad_out.data_ptr(), x_flat.data_ptr(), W.data_ptr(),
-                     proj_out.data_ptr(), inv_rms.data_ptr(), grad_x.data_ptr(), T, nC, D_out,
-                     _stream(x_flat))
-        grad_W = _k1_grad_w(grad_out, x_flat, inv_rms, D_out)
+        ws_bytes = _native.workspace_size_k1_bwd(T, nC, D_out)
+        ws = torch.empty(max(ws_bytes, 1), device=x_flat.device, dtype=torch.uint8)
+        _native.call("fmhc_k1_bwd", grad_out.data_ptr(), x_flat.data_ptr(), W.data_ptr(),
+                     proj_out.data_ptr(), inv_rms.data_ptr(), grad_x.data_ptr(),
+                     grad_W.data_ptr(), ws.data_ptr(), ws_bytes, T, nC, D_out, _stream(x_flat))
     return grad_x, grad_W
 
 

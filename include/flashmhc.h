@@ -88,19 +88,23 @@ FMHC_API int fmhc_k1_bwd_dx(const void *grad_out, const void *x, const void *W,
                    int64_t T, int64_t nC, int64_t D, void *stream);
 
 /* ------------------------------------------------------------------------
- * K1 weight gradient.
+ * K1 backward, grad_x AND grad_W in one pass over x.
+ *   grad_x as fmhc_k1_bwd_dx;
  *   grad_W[d,k] = bf16( sum_t bf16(go[t,d] * inv_rms[t]) * x[t,k] )   f32 accumulate
- * grad_out (T, D) bf16, x (T, nC) bf16, inv_rms (T,) f32 -> grad_W (D, nC) bf16.
+ * -> grad_x (T, nC) bf16, grad_W (D, nC) bf16.
  * `workspace` is caller-owned device memory of at least
- * fmhc_k1_bwd_dw_workspace_size(T, nC, D) bytes (256-byte aligned); its
- * contents on entry do not matter.
- * Replaces the cuBLAS matmul in the K1 autograd formula
- * (src/flash_mhc/ops.py:683-684).
+ * fmhc_k1_bwd_workspace_size(T, nC, D) bytes (256-byte aligned; the size
+ * depends on the current device's SM count); its contents on entry do not
+ * matter and the result does not depend on them (the grad_W reduction order
+ * is fixed, so results are bitwise reproducible).
+ * Replaces the K1 autograd formula (src/flash_mhc/ops.py:678-685): the
+ * bwd-dx op plus the separate cuBLAS matmul for grad_W (ops.py:683-684).
  */
-FMHC_API int64_t fmhc_k1_bwd_dw_workspace_size(int64_t T, int64_t nC, int64_t D);
-FMHC_API int fmhc_k1_bwd_dw(const void *grad_out, const void *x, const float *inv_rms,
-                   void *grad_W, void *workspace, int64_t workspace_bytes,
-                   int64_t T, int64_t nC, int64_t D, void *stream);
+FMHC_API int64_t fmhc_k1_bwd_workspace_size(int64_t T, int64_t nC, int64_t D);
+FMHC_API int fmhc_k1_bwd(const void *grad_out, const void *x, const void *W,
+                         const void *proj, const float *inv_rms, void *grad_x,
+                         void *grad_W, void *workspace, int64_t workspace_bytes,
+                         int64_t T, int64_t nC, int64_t D, void *stream);
 
 /* ------------------------------------------------------------------------
  * K3 forward: pre-map of the n streams into the layer input.

@@ -23,7 +23,7 @@ def _declared():
 
 def test_header_declares_entry_points():
     names = _declared()
-    for must in ("fmhc_k1_fwd", "fmhc_k1_bwd_dx", "fmhc_k1_bwd_dw", "fmhc_k3_fwd",
+    for must in ("fmhc_k1_fwd", "fmhc_k1_bwd_dx", "fmhc_k1_bwd", "fmhc_k3_fwd",
                  "fmhc_k3_bwd", "fmhc_k4_fwd", "fmhc_k4_bwd", "fmhc_last_error"):
         assert must in names
 
@@ -59,7 +59,7 @@ def test_argument_validation_without_gpu():
     st, msg = _status("fmhc_k4_fwd", p, p, ctypes.c_void_p(20), p, p, 8, 4, 64, None)
     assert st == 3 and "16-byte" in msg
     ws = ctypes.c_void_p(4096)
-    st, msg = _status("fmhc_k1_bwd_dw", p, p, p, p, ws, 0, 8, 256, 32, None)
+    st, msg = _status("fmhc_k1_bwd", p, p, p, p, p, p, p, ws, 0, 8, 256, 32, None)
     assert st == 6 and "workspace" in msg
     # T == 0 is a no-op that succeeds without touching the device
     st, msg = _status("fmhc_k4_bwd", None, None, None, None, None, None, None, None, None,
@@ -74,6 +74,6 @@ def test_python_raises_value_error_for_invalid_argument():
 
 
 def test_workspace_size_query():
-    assert _native.workspace_size_k1_dw(0, 4096, 32) == 0
-    n = _native.workspace_size_k1_dw(65536, 4096, 32)
+    assert _native.workspace_size_k1_bwd(0, 4096, 32) == 0
+    n = _native.workspace_size_k1_bwd(65536, 4096, 32)
     assert n > 0 and n % 256 == 0

@@ -154,6 +154,13 @@ def test_eval_no_grad_tiny_T_with_outliers(T):
                   bias=blk.W_all.bias.detach().float().cpu().numpy(),
                   perm=blk.perm_mat.float().cpu().numpy(),
                   Wl=blk.layer.weight.detach().float().cpu().numpy())
-    r = O.block_forward_backward(params, xb.float().cpu().numpy(), np.zeros((T, 4, C)),
-                                 rms_eps=1e-6, layer="linear")
-    assert_close("out vs oracle", out.float().cpu().numpy(), r["out"], 5e-2, 2e-2)
+    xn = xb.float().cpu().numpy()
+    r = O.block_forward_backward(params, xn, np.zeros((T, 4, C)), rms_eps=1e-6, layer="linear")
+    # K2 runs in bf16 (as in the reference), so H_merged and h_post carry an
+    # absolute error of ~2^-8; with x100 outlier channels that error is
+    # multiplied by |x|.  Bound: 5e-2 + 2e-2*|ref| + 2^-7 * (sum_j |x_j| + |lo|).
+    got = out.float().cpu().numpy()
+    cond = np.abs(xn).sum(axis=1, keepdims=True) + np.abs(r["layer_input"] @ params["Wl"].T)[:, None, :]
+    lim = 5e-2 + 2e-2 * np.abs(r["out"]) + 2.0 ** -7 * cond
+    diff = np.abs(got - r["out"])
+    assert np.all(diff <= lim), f"out vs oracle: worst {np.max(diff / lim):.3g} x bound"

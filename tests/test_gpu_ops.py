@@ -18,6 +18,7 @@ import numpy as np
 import pytest
 import torch
 
+import flash_mhc  # noqa: F401  (registers torch.ops.flash_mhc)
 from oracle import mhc_oracle as O
 from tests._util import assert_close, assert_sum_close, load_golden
 
@@ -245,24 +246,41 @@ def _kernel_names(fn):
 
 
 def test_metric_shape_runs_the_tensor_core_k1():
-    """At T=65536, nC=4096 the K1 forward is the TMA + tcgen05 kernel."""
+    """At T=65536, nC=4096 the K1 forward and backward are the TMA + tcgen05 kernels."""
     d = _inputs(256, 1024, 9)
     xf = torch.randn(65536, 4096, device="cuda").bfloat16()
     W = _bf(np.tile(d["W"], (1, 1)))
     names = _kernel_names(lambda: torch.ops.flash_mhc.fused_rmsnorm_project(xf, W))
     assert any("k1_fwd_tc_kernel" in n for n in names), names
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
+    go = torch.randn(65536, 32, device="cuda").bfloat16()
+    names = _kernel_names(
+        lambda: torch.ops.flash_mhc.fused_rmsnorm_project_backward(go, xf, W, out, inv))
+    assert any("k1_bwd_tc_kernel" in n for n in names), names
 
 
-@pytest.mark.parametrize("T", [1, 31, 33, 1000, 4733])
-def test_k1_fwd_token_partitioning(T):
-    """Token ranges split across CTAs in 32-row units, partial tiles and boxes."""
-    C = 256
+@pytest.mark.parametrize("T,C", [(1, 256), (31, 256), (33, 256), (1000, 256), (4733, 256),
+                                 (3000, 1024), (129, 2048)])
+def test_k1_token_partitioning(T, C):
+    """Forward: token ranges split across CTAs in 32-row units, partial tiles.
+    Backward: (k-chunk, token-tile) unit runs per CTA that cross k-chunk
+    segments, fewer units than SMs, partial token tiles; grad_W reduction."""
     d = _inputs(T, C, 40 + T)
     xf_np = d["x"].reshape(T, 4 * C)
-    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(_bf(xf_np), _bf(d["W"]))
+    xf, W, go = _bf(xf_np), _bf(d["W"]), _bf(d["g_proj"])
+    out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
     rout, rinv = O.k1_fwd(xf_np, d["W"])
     assert_close("inv_rms", _np(inv), rinv, 0, 1e-5)
     assert_close("out", _np(out), rout, BF_ATOL, BF_RTOL)
+    gx, gW = torch.ops.flash_mhc.fused_rmsnorm_project_backward(go, xf, W, out, inv)
+    rgx = O.k1_bwd_dx(d["g_proj"], xf_np, d["W"], _np(out), _np(inv))
+    assert_close("gx", _np(gx), rgx, BF_ATOL, BF_RTOL)
+    _check_gw(_np(gW), d["g_proj"], xf_np, _np(inv))
+    gx_only = torch.ops.flash_mhc.fused_rmsnorm_project_bwd_dx(go, xf, W, out, inv)
+    assert torch.equal(gx_only, gx)
+    # deterministic: a second call gives identical bits
+    gx2, gW2 = torch.ops.flash_mhc.fused_rmsnorm_project_backward(go, xf, W, out, inv)
+    assert torch.equal(gx2, gx) and torch.equal(gW2, gW)
 
 
 def test_no_device_error_recorded():
