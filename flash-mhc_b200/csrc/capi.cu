@@ -61,6 +61,11 @@ int check_streams(const char *what, int64_t T, int64_t n, int64_t C) {
 
 }  // namespace
 
+namespace fmhc {
+// Records `msg` as this thread's fmhc_last_error() text and returns `code`.
+int set_last_error(int code, const char *msg) { return fail(code, "%s", msg); }
+}  // namespace fmhc
+
 extern "C" {
 
 const char *fmhc_last_error(void) { return g_err; }

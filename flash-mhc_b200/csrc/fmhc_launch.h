@@ -7,6 +7,9 @@
 
 namespace fmhc {
 
+// capi.cu -- sets this thread's fmhc_last_error() text, returns `code`.
+int set_last_error(int code, const char *msg);
+
 // k3k4_stream.cu -- `vec` is the bf16 chunk width (8, 4, 2 or 1).
 void launch_k3_fwd(const void *x, const float *hp, void *out, int64_t T, int C, int vec,
                    cudaStream_t s);

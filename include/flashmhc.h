@@ -107,6 +107,30 @@ FMHC_API int fmhc_k1_bwd(const void *grad_out, const void *x, const void *W,
                          int64_t T, int64_t nC, int64_t D, void *stream);
 
 /* ------------------------------------------------------------------------
+ * K1 backward without a caller workspace: same inputs, outputs and results as
+ * fmhc_k1_bwd, but the scratch comes from a fixed 32 MiB array inside the
+ * library, so this call allocates no memory and needs none from the caller.
+ * For callers that cannot allocate device memory: hosts that only hold
+ * pointers handed to them and have no device allocator of their own (C, Go or
+ * Java code calling through this ABI, plugins inside another framework's
+ * memory pool), serving runtimes that reserve all HBM up front, and
+ * latency-critical paths where cudaMalloc (which can synchronise the device)
+ * is not allowed.
+ * Limit: fmhc_k1_bwd_workspace_size(T, nC, D) must not exceed 32 MiB (this
+ * covers, e.g., T = 131072 tokens at nC = 16384); larger calls fail with
+ * FMHC_ERR_WORKSPACE and should use fmhc_k1_bwd.  Every GPU that loads the
+ * library holds the 32 MiB until the process exits.  The first call on each
+ * device looks up the array's device address; make it before any stream
+ * capture.  All calls share the array, so calls that overlap on the same GPU
+ * race and must not be issued; the array's previous contents never matter.
+ * No counterpart in the reference (its ops always allocate through torch).
+ */
+FMHC_API int fmhc_k1_bwd_noalloc(const void *grad_out, const void *x, const void *W,
+                                 const void *proj, const float *inv_rms, void *grad_x,
+                                 void *grad_W, int64_t T, int64_t nC, int64_t D,
+                                 void *stream);
+
+/* ------------------------------------------------------------------------
  * K3 forward: pre-map of the n streams into the layer input.
  *   out[t,c] = bf16( sum_j h_pre[t,j] * x[t,j,c] )
  * x (T, n, C) bf16, h_pre (T, n) f32 -> out (T, C) bf16.
