@@ -51,7 +51,12 @@ struct alignas(1024) BwdSmem {
   uint64_t wempty[2];
   uint64_t dwfull;
   uint64_t dwempty;
-  uint64_t epi;       // the 4 epilogue warps finished writing grad_x of a unit
+  // epi[i & 1]: the 4 epilogue warps finished writing grad_x of local unit i.
+  // Two barriers, and each warp arrives on it before it releases the unit's
+  // TMEM accumulator: a warp can then never arrive for unit i + 2 before every
+  // warp arrived for unit i (unit i + 2 needs that accumulator back), so each
+  // phase counts exactly the four arrivals of one unit.
+  uint64_t epi[2];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -110,7 +115,8 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
     mbar_init(smem_u32(&sm.dwfull), 1);
     mbar_init(smem_u32(&sm.dwempty), 4);
-    mbar_init(smem_u32(&sm.epi), 4);
+    mbar_init(smem_u32(&sm.epi[0]), 4);
+    mbar_init(smem_u32(&sm.epi[1]), 4);
     mbar_init(smem_u32(&sm.mma_done), 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -232,8 +238,10 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     const int r = q * 32 + lane;  // token row of the unit / k row of the grad_W partial
     const bool leader = (warp == 2 && lane == 0);
     int stage = 0, acc = 0, seg = -1, kc_prev = -1, prev_stage = -1;
-    uint32_t phase = 0, acc_phase = 0, epi_phase = 0;
+    uint32_t phase = 0, acc_phase = 0;
     for (int64_t u = u0; u < u1 && !*abort; ++u) {
+      const int64_t li = u - u0;  // local unit index
+      const uint32_t epi_bar = smem_u32(&sm.epi[li & 1]);
       int kc, tt;
       bwd_unit(u, a.ntt, kc, tt);
       if (kc != kc_prev) { ++seg; kc_prev = kc; }
@@ -283,16 +291,18 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           *p = o;
         }
       }
+      // Every writer makes its grad_x visible to the TMA (async proxy), then
+      // one arrive per warp on epi (before the TMEM release, see BwdSmem);
+      // only the store-issuing thread waits (bounded).
+      fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.tempty[acc]));
-      // Every writer makes its grad_x visible to the TMA (async proxy), then
-      // one arrive per warp; only the store-issuing thread waits (bounded).
-      fence_proxy_async_smem();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(smem_u32(&sm.epi));
+      if (lane == 0) {
+        mbar_arrive(epi_bar);
+        mbar_arrive(smem_u32(&sm.tempty[acc]));
+      }
       if (leader) {
-        if (!mbar_wait(smem_u32(&sm.epi), epi_phase, abort, kSiteBEpiStore)) break;
+        if (!mbar_wait(epi_bar, uint32_t(li >> 1) & 1u, abort, kSiteBEpiStore)) break;
         const uint32_t base = smem_u32(xs);
         tma_store_2d(&tmap_gx, base, kc * kBwdBK, tt * kBwdBT);
         tma_store_2d(&tmap_gx, base + kBwdXBox, kc * kBwdBK + 64, tt * kBwdBT);
@@ -302,7 +312,6 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         if (prev_stage >= 0) mbar_arrive(smem_u32(&sm.empty[prev_stage]));
         prev_stage = stage;
       }
-      epi_phase ^= 1;
       if (a.with_dw && last_in_seg) {
         // grad_W partial of this segment: thread r owns k row r, 32 d columns.
         if (!mbar_wait(smem_u32(&sm.dwfull), seg & 1, abort, kSiteBEpiDw)) break;

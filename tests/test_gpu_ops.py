@@ -288,3 +288,27 @@ def test_no_device_error_recorded():
     from flash_mhc import _native
 
     assert _native.check_device_error() == 0
+
+
+def test_k1_tensor_core_kernels_are_bitwise_deterministic_at_metric_shape():
+    """Repeated runs at T=65536, nC=4096 give identical bits (fixed reduction
+    orders, no atomics); a race between pipeline roles would show up here."""
+    torch.manual_seed(3)
+    xf = torch.randn(65536, 4096, device="cuda").bfloat16()
+    W = (torch.randn(32, 4096, device="cuda") * 0.02).bfloat16()
+    go = torch.randn(65536, 32, device="cuda").bfloat16()
+    out0, inv0 = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
+    gx0, gW0 = torch.ops.flash_mhc.fused_rmsnorm_project_backward(go, xf, W, out0, inv0)
+    for _ in range(8):
+        out, inv = torch.ops.flash_mhc.fused_rmsnorm_project(xf, W)
+        gx, gW = torch.ops.flash_mhc.fused_rmsnorm_project_backward(go, xf, W, out0, inv0)
+        assert torch.equal(out, out0) and torch.equal(inv, inv0)
+        assert torch.equal(gx, gx0) and torch.equal(gW, gW0)
+    rinv = torch.rsqrt((xf.float() ** 2).mean(1) + 1e-6)
+    torch.testing.assert_close(inv0, rinv, atol=0, rtol=1e-5)
+    s = (go.float() * out0.float()).sum(1) * inv0 * inv0 / 4096
+    rgx = inv0[:, None] * (go.float() @ W.float()) - s[:, None] * xf.float()
+    torch.testing.assert_close(gx0.float(), rgx, atol=BF_ATOL, rtol=BF_RTOL)
+    gos = (go.float() * inv0[:, None]).bfloat16().float()
+    rgW = gos.t() @ xf.float()
+    torch.testing.assert_close(gW0.float(), rgW, atol=BF_ATOL, rtol=BF_RTOL)
