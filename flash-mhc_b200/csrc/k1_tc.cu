@@ -365,7 +365,7 @@ namespace {
 struct BwdPlan {
   int ntt, nkc, grid, maxseg;
   int64_t units;
-  int64_t gos_bytes, part_bytes;
+  int64_t gos_bytes, sinv_bytes, part_bytes;
 };
 
 int64_t round256(int64_t b) { return (b + 255) & ~int64_t(255); }
@@ -387,6 +387,7 @@ BwdPlan bwd_plan(int64_t T, int64_t nC) {
     if (segs > p.maxseg) p.maxseg = segs;
   }
   p.gos_bytes = round256(T * kND * 2);
+  p.sinv_bytes = round256(int64_t(p.ntt) * kBwdBT * 8);
   p.part_bytes = round256(int64_t(p.grid) * p.maxseg * kND * kBwdBK * 4);
   return p;
 }
@@ -407,7 +408,7 @@ bool k1_tc_bwd_supported(const void *go, const void *x, const void *W, const voi
 int64_t k1_tc_bwd_workspace_bytes(int64_t T, int64_t nC) {
   if (T < 1 || nC % k1tc::kBwdBK) return 0;
   const k1tc::BwdPlan p = k1tc::bwd_plan(T, nC);
-  return p.gos_bytes + p.part_bytes;
+  return p.gos_bytes + p.sinv_bytes + p.part_bytes;
 }
 
 int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *proj,
@@ -417,16 +418,18 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   const BwdPlan p = bwd_plan(T, nC);
   const bool with_dw = gW != nullptr;
   uint8_t *gos = nullptr;
+  float2 *sinv = nullptr;
   float *part = nullptr;
   if (with_dw) {
-    if (ws == nullptr || ws_bytes < p.gos_bytes + p.part_bytes ||
-        (reinterpret_cast<uintptr_t>(ws) & 255)) {
+    const int64_t need = p.gos_bytes + p.sinv_bytes + p.part_bytes;
+    if (ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)) {
       snprintf(g_msg, sizeof(g_msg), "workspace of %lld bytes (need %lld, 256-byte aligned)",
-               (long long)ws_bytes, (long long)(p.gos_bytes + p.part_bytes));
+               (long long)ws_bytes, (long long)need);
       return 6;
     }
     gos = static_cast<uint8_t *>(ws);
-    part = reinterpret_cast<float *>(gos + p.gos_bytes);
+    sinv = reinterpret_cast<float2 *>(gos + p.gos_bytes);
+    part = reinterpret_cast<float *>(gos + p.gos_bytes + p.sinv_bytes);
   }
   CUtensorMap mx, mgx, mgo, mgos, mw;
   bool ok = make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBwdBT,
@@ -443,9 +446,10 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
     return 5;
   }
   if (with_dw) {
-    const int64_t n8 = T * (kND / 8);
-    k1_bwd_gos_kernel<<<unsigned((n8 + 255) / 256), 256, 0, s>>>(
-        static_cast<const __nv_bfloat16 *>(go), inv_rms, reinterpret_cast<__nv_bfloat16 *>(gos), T);
+    const int64_t T_pad = int64_t(p.ntt) * kBwdBT;
+    k1_bwd_prep_kernel<<<unsigned((T_pad + 255) / 256), 256, 0, s>>>(
+        static_cast<const __nv_bfloat16 *>(go), static_cast<const __nv_bfloat16 *>(proj), inv_rms,
+        reinterpret_cast<__nv_bfloat16 *>(gos), sinv, T, T_pad, nC);
   }
   const size_t smem = sizeof(BwdSmem) + 1024;
   if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_bwd_tc_kernel), smem)) return e;
@@ -453,6 +457,7 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.go = static_cast<const __nv_bfloat16 *>(go);
   args.proj = static_cast<const __nv_bfloat16 *>(proj);
   args.inv_rms = inv_rms;
+  args.sinv = sinv;
   args.dw_part = part;
   args.T = T;
   args.nC = nC;
@@ -460,7 +465,7 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.units = p.units;
   args.maxseg = p.maxseg;
   args.with_dw = with_dw ? 1 : 0;
-  k1_bwd_tc_kernel<<<unsigned(p.grid), kThreads, smem, s>>>(mx, mgx, mgo, mgos, mw, args);
+  k1_bwd_tc_kernel<<<unsigned(p.grid), kBwdThreads, smem, s>>>(mx, mgx, mgo, mgos, mw, args);
   if (with_dw) {
     const int64_t n = int64_t(kND) * nC;
     k1_bwd_dw_reduce_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(

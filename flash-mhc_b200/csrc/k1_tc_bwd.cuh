@@ -19,11 +19,17 @@
 //                        8 x M128 N32 K16, accumulated over the segment;
 //                grad_x: D1[t, k]  = go (K-major A) * W^T (MN-major B),
 //                        2 x M128 N128 K16 into one of two TMEM buffers.
-//   warps 2-5  one thread per token row: grad_x = inv*D1 - s*x written over x
-//              in the stage buffer, then stored by TMA; at a segment end the
-//              grad_W partial D2 (thread per k row) goes to the workspace.
-// A second small kernel reduces the per-CTA grad_W partials in a fixed order
-// (deterministic) and rounds to bf16.
+//   warps 2-9  epilogue, two warps per TMEM lane quarter: thread = token row,
+//              warps 2-5 columns 0-63, warps 6-9 columns 64-127 of the unit:
+//              grad_x = inv*D1 - s*x written over x in the stage buffer, then
+//              stored by TMA; at a segment end warps 2-5 move the grad_W
+//              partial D2 (thread per k row) to the workspace.
+// A prep kernel computes per token s and inv_rms (float2) and the grad_W
+// operand gos; the producer brings the unit's 128 (s, inv) pairs into the
+// stage with a bulk copy, so the epilogue reads them from shared memory.  A
+// final small kernel reduces the per-CTA grad_W partials in a fixed order
+// (deterministic) and rounds to bf16.  Without a workspace (grad_x only) the
+// epilogue computes s itself from go and proj.
 #pragma once
 
 namespace fmhc {
@@ -35,7 +41,10 @@ constexpr int kBwdStages = 4;
 constexpr int kBwdXBytes = kBwdBT * kBwdBK * 2;   // 32 KiB (two 16 KiB boxes)
 constexpr int kBwdXBox = kBwdBT * 64 * 2;         // 16 KiB
 constexpr int kBwdGBytes = kBwdBT * kND * 2;      // 8 KiB  (go or gos tile)
-constexpr int kBwdStageBytes = kBwdXBytes + 2 * kBwdGBytes;  // 48 KiB
+constexpr int kBwdSBytes = kBwdBT * 8;            // 1 KiB  ((s, inv_rms) per token)
+constexpr int kBwdStageBytes = kBwdXBytes + 2 * kBwdGBytes + kBwdSBytes;  // 49 KiB
+constexpr int kBwdThreads = 320;                  // producer, MMA, 8 epilogue warps
+constexpr int kBwdEpiWarps = 8;
 constexpr int kBwdWBytes = kND * kBwdBK * 2;      // 8 KiB  (two 4 KiB boxes)
 constexpr uint32_t kBwdTmemCols = 512;            // 2 x 128 (grad_x) + 32 (grad_W)
 constexpr uint32_t kBwdDwCol = 256;
@@ -71,6 +80,7 @@ struct BwdArgs {
   const __nv_bfloat16 *go;    // (T, 32)
   const __nv_bfloat16 *proj;  // (T, 32)
   const float *inv_rms;       // (T,)
+  const float2 *sinv;         // (ntt*128,) (s, inv_rms) per token, or nullptr
   float *dw_part;             // [grid][maxseg][32][128] f32 (only with_dw)
   int64_t T;
   int nC;
@@ -86,7 +96,7 @@ __device__ __forceinline__ void bwd_unit(int64_t u, int ntt, int &kc, int &tt) {
   tt = int(u - int64_t(kc) * ntt);
 }
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, 1)
 k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_gx,
                  const __grid_constant__ CUtensorMap tmap_go,
@@ -109,14 +119,14 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&sm.tfull[b]), 1);
-      mbar_init(smem_u32(&sm.tempty[b]), 4);
+      mbar_init(smem_u32(&sm.tempty[b]), kBwdEpiWarps);
       mbar_init(smem_u32(&sm.wfull[b]), 1);
       mbar_init(smem_u32(&sm.wempty[b]), 1);
     }
     mbar_init(smem_u32(&sm.dwfull), 1);
-    mbar_init(smem_u32(&sm.dwempty), 4);
-    mbar_init(smem_u32(&sm.epi[0]), 4);
-    mbar_init(smem_u32(&sm.epi[1]), 4);
+    mbar_init(smem_u32(&sm.dwempty), 4);  // warps 2-5 read the grad_W partial
+    mbar_init(smem_u32(&sm.epi[0]), kBwdEpiWarps);
+    mbar_init(smem_u32(&sm.epi[1]), kBwdEpiWarps);
     mbar_init(smem_u32(&sm.mma_done), 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -140,7 +150,8 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     if (lane == 0) {
       int stage = 0, issued = 0, seg = -1, kc_prev = -1;
       uint32_t phase = 0;
-      const uint32_t tx = uint32_t(kBwdXBytes + (a.with_dw ? 2 : 1) * kBwdGBytes);
+      const uint32_t tx = uint32_t(kBwdXBytes + (a.with_dw ? 2 : 1) * kBwdGBytes +
+                                   (a.sinv ? kBwdSBytes : 0));
       for (int64_t u = u0; u < u1 && !*abort; ++u) {
         int kc, tt;
         bwd_unit(u, a.ntt, kc, tt);
@@ -163,6 +174,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         tma_load_2d(base + kBwdXBox, &tmap_x, f, kc * kBwdBK + 64, row0);
         tma_load_2d(base + kBwdXBytes, &tmap_go, f, 0, row0);
         if (a.with_dw) tma_load_2d(base + kBwdXBytes + kBwdGBytes, &tmap_gos, f, 0, row0);
+        if (a.sinv) bulk_load(base + kBwdXBytes + 2 * kBwdGBytes, a.sinv + row0, kBwdSBytes, f);
         ++issued;
         if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
       }
@@ -234,8 +246,9 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
   } else {
     // ------------------------------------------------------------ epilogue
-    const int q = warp & 3;
-    const int r = q * 32 + lane;  // token row of the unit / k row of the grad_W partial
+    const int q = warp & 3;           // TMEM lane quarter
+    const int h = (warp - 2) >> 2;    // column half of the unit (0: 0-63, 1: 64-127)
+    const int r = q * 32 + lane;      // token row of the unit / k row of the grad_W partial
     const bool leader = (warp == 2 && lane == 0);
     int stage = 0, acc = 0, seg = -1, kc_prev = -1, prev_stage = -1;
     uint32_t phase = 0, acc_phase = 0;
@@ -251,8 +264,8 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 
       const int64_t t = int64_t(tt) * kBwdBT + r;
       float s = 0.f, inv = 0.f;
-      if (t < a.T) {
-        // s = (go . proj) * inv^2 / nC from the stored forward output.
+      if (!a.sinv && t < a.T) {
+        // No workspace: s = (go . proj) * inv^2 / nC from the stored forward output.
         inv = a.inv_rms[t];
         const uint4 *g4 = reinterpret_cast<const uint4 *>(a.go + t * kND);
         const uint4 *p4 = reinterpret_cast<const uint4 *>(a.proj + t * kND);
@@ -268,21 +281,29 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         s = dot * (inv * inv) / float(a.nC);
       }
       if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteBEpiFull)) break;
+      uint8_t *xs = sm.stage[stage];
+      if (a.sinv) {
+        const float2 si = reinterpret_cast<const float2 *>(xs + kBwdXBytes + 2 * kBwdGBytes)[r];
+        s = si.x;
+        inv = si.y;
+      }
       if (!mbar_wait(smem_u32(&sm.tfull[acc]), acc_phase, abort, kSiteBEpiTfull)) break;
       tc_fence_after();
-      uint8_t *xs = sm.stage[stage];
+      uint32_t v[2][32];
+      const uint32_t tl = tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * kBwdBK + 64 * h);
+      tmem_ld_32x32b_x32(tl, v[0]);
+      tmem_ld_32x32b_x32(tl + 32, v[1]);
+      tmem_wait_ld();
+      // Columns 64h .. 64h+63 of row r are one 128-byte row of x box h.
+      uint8_t *rowp = xs + h * kBwdXBox + r * 128;
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        uint32_t v[32];
-        tmem_ld_32x32b_x32(tmem + (uint32_t(q * 32) << 16) + uint32_t(acc * kBwdBK + 32 * j), v);
-        tmem_wait_ld();
-        uint8_t *rowp = xs + (j >> 1) * kBwdXBox + r * 128;
+      for (int j = 0; j < 2; ++j) {
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
-          const int chunk = ((j & 1) * 4 + c) ^ (r & 7);
+          const int chunk = (j * 4 + c) ^ (r & 7);
           uint4 *p = reinterpret_cast<uint4 *>(rowp + chunk * 16);
           const uint4 xv = *p;
-          const float *dv = reinterpret_cast<const float *>(v + 8 * c);
+          const float *dv = reinterpret_cast<const float *>(v[j] + 8 * c);
           uint4 o;
           o.x = pack_bf16x2(fmaf(-s, bf16lo(xv.x), inv * dv[0]), fmaf(-s, bf16hi(xv.x), inv * dv[1]));
           o.y = pack_bf16x2(fmaf(-s, bf16lo(xv.y), inv * dv[2]), fmaf(-s, bf16hi(xv.y), inv * dv[3]));
@@ -312,7 +333,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         if (prev_stage >= 0) mbar_arrive(smem_u32(&sm.empty[prev_stage]));
         prev_stage = stage;
       }
-      if (a.with_dw && last_in_seg) {
+      if (a.with_dw && last_in_seg && h == 0) {
         // grad_W partial of this segment: thread r owns k row r, 32 d columns.
         if (!mbar_wait(smem_u32(&sm.dwfull), seg & 1, abort, kSiteBEpiDw)) break;
         tc_fence_after();
@@ -344,22 +365,42 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
-// gos[t, d] = bf16(go[t, d] * inv_rms[t]): the grad_W operand, rounded like
-// the reference's (grad_out * inv_rms).to(x.dtype).  One thread per 8 values.
-__global__ void k1_bwd_gos_kernel(const __nv_bfloat16 *__restrict__ go,
-                                  const float *__restrict__ inv_rms,
-                                  __nv_bfloat16 *__restrict__ gos, int64_t T) {
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;  // chunk of 8
-  if (i >= T * (kND / 8)) return;
-  const int64_t t = i / (kND / 8);
+// Per token: sinv[t] = (s, inv_rms) with s = (go . proj) * inv_rms^2 / nC,
+// and (when gos != nullptr) gos[t, :] = bf16(go[t, :] * inv_rms[t]), the
+// grad_W operand, rounded like the reference's (grad_out * inv_rms).to(x.dtype).
+// One thread per token; rows T .. T_pad-1 of sinv are zeroed.
+__global__ void k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go,
+                                   const __nv_bfloat16 *__restrict__ proj,
+                                   const float *__restrict__ inv_rms,
+                                   __nv_bfloat16 *__restrict__ gos, float2 *__restrict__ sinv,
+                                   int64_t T, int64_t T_pad, int nC) {
+  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= T_pad) return;
+  if (t >= T) {
+    sinv[t] = make_float2(0.f, 0.f);
+    return;
+  }
   const float r = inv_rms[t];
-  const uint4 g = __ldg(reinterpret_cast<const uint4 *>(go) + i);
-  uint4 o;
-  o.x = pack_bf16x2(bf16lo(g.x) * r, bf16hi(g.x) * r);
-  o.y = pack_bf16x2(bf16lo(g.y) * r, bf16hi(g.y) * r);
-  o.z = pack_bf16x2(bf16lo(g.z) * r, bf16hi(g.z) * r);
-  o.w = pack_bf16x2(bf16lo(g.w) * r, bf16hi(g.w) * r);
-  reinterpret_cast<uint4 *>(gos)[i] = o;
+  const uint4 *g4 = reinterpret_cast<const uint4 *>(go + t * kND);
+  const uint4 *p4 = reinterpret_cast<const uint4 *>(proj + t * kND);
+  float dot = 0.f;
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 g = __ldg(g4 + c), p = __ldg(p4 + c);
+    dot = fmaf(bf16lo(g.x), bf16lo(p.x), dot); dot = fmaf(bf16hi(g.x), bf16hi(p.x), dot);
+    dot = fmaf(bf16lo(g.y), bf16lo(p.y), dot); dot = fmaf(bf16hi(g.y), bf16hi(p.y), dot);
+    dot = fmaf(bf16lo(g.z), bf16lo(p.z), dot); dot = fmaf(bf16hi(g.z), bf16hi(p.z), dot);
+    dot = fmaf(bf16lo(g.w), bf16lo(p.w), dot); dot = fmaf(bf16hi(g.w), bf16hi(p.w), dot);
+    if (gos) {
+      uint4 o;
+      o.x = pack_bf16x2(bf16lo(g.x) * r, bf16hi(g.x) * r);
+      o.y = pack_bf16x2(bf16lo(g.y) * r, bf16hi(g.y) * r);
+      o.z = pack_bf16x2(bf16lo(g.z) * r, bf16hi(g.z) * r);
+      o.w = pack_bf16x2(bf16lo(g.w) * r, bf16hi(g.w) * r);
+      reinterpret_cast<uint4 *>(gos + t * kND)[c] = o;
+    }
+  }
+  sinv[t] = make_float2(dot * (r * r) / float(nC), r);
 }
 
 // grad_W[d, k] = bf16(sum of the partials of every CTA whose unit range
