@@ -35,21 +35,33 @@ namespace k1tc {
 
 using namespace sm100;
 
+// A stage holds kColBoxes column boxes of 64 k (one 128-byte swizzled row
+// each) for up to 128 rows, so every x row is read kColBoxes * 128 contiguous
+// bytes at a time.
+#ifndef FMHC_K1F_COLBOXES
+#define FMHC_K1F_COLBOXES 2
+#endif
+#ifndef FMHC_K1F_STAGES
+#define FMHC_K1F_STAGES (FMHC_K1F_COLBOXES == 1 ? 8 : 5)
+#endif
 constexpr int kBM = 128;            // tile rows (MMA M)
-constexpr int kBK = 64;             // k per stage: one 128-byte swizzled row
+constexpr int kColBoxes = FMHC_K1F_COLBOXES;
+constexpr int kBK = 64 * kColBoxes; // k per stage
 constexpr int kND = 32;             // projection width (MMA N)
 constexpr int kBoxRows = 32;        // TMA box rows for x
-constexpr int kStages = 8;
-constexpr int kABytes = kBM * kBK * 2;        // 16 KiB
-constexpr int kBBytes = kND * kBK * 2;        // 4 KiB
-constexpr int kBoxBytes = kBoxRows * kBK * 2; // 4 KiB
+constexpr int kStages = FMHC_K1F_STAGES;
+constexpr int kColABytes = kBM * 64 * 2;       // 16 KiB: one column box, 128 rows
+constexpr int kColBBytes = kND * 64 * 2;       // 4 KiB: one W column box
+constexpr int kABytes = kColBoxes * kColABytes;
+constexpr int kBBytes = kColBoxes * kColBBytes;
+constexpr int kBoxBytes = kBoxRows * 64 * 2;   // 4 KiB: 32 rows of one column box
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 192;
 constexpr uint32_t kTmemCols = 64;  // two 32-column accumulators
 constexpr float kEps = 1e-6f;
 
 struct alignas(1024) FwdSmem {
-  uint8_t stage[kStages][kStageBytes];  // 20 KiB each, 1 KiB aligned
+  uint8_t stage[kStages][kStageBytes];  // kColBoxes x 20 KiB each, 1 KiB aligned
   uint64_t full[kStages];
   uint64_t empty[kStages];
   uint64_t tfull[2];
@@ -119,11 +131,15 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, abort, kSiteProdEmpty)) break;
           const uint32_t full = smem_u32(&sm.full[stage]);
-          mbar_arrive_expect_tx(full, uint32_t(nbox * kBoxBytes + kBBytes));
+          mbar_arrive_expect_tx(full, uint32_t(kColBoxes * (nbox * kBoxBytes + kColBBytes)));
           const uint32_t a = smem_u32(sm.stage[stage]);
-          for (int b = 0; b < nbox; ++b)
-            tma_load_2d(a + b * kBoxBytes, &tmap_x, full, kb * kBK, int32_t(row0 + b * kBoxRows));
-          tma_load_2d(a + kABytes, &tmap_w, full, kb * kBK, 0);
+          for (int cb = 0; cb < kColBoxes; ++cb) {
+            const int32_t k0 = kb * kBK + cb * 64;
+            for (int b = 0; b < nbox; ++b)
+              tma_load_2d(a + cb * kColABytes + b * kBoxBytes, &tmap_x, full, k0,
+                          int32_t(row0 + b * kBoxRows));
+            tma_load_2d(a + kABytes + cb * kColBBytes, &tmap_w, full, k0, 0);
+          }
           ++issued;
           if (++stage == kStages) { stage = 0; phase ^= 1; }
         }
@@ -156,8 +172,9 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           const uint32_t a = smem_u32(sm.stage[stage]);
 #pragma unroll
           for (int k = 0; k < kBK / 16; ++k) {
-            const uint64_t ad = smem_desc(a + k * 32, 16, 1024, 2);
-            const uint64_t bd = smem_desc(a + kABytes + k * 32, 16, 1024, 2);
+            const int cb = k / 4, kk = k % 4;
+            const uint64_t ad = smem_desc(a + cb * kColABytes + kk * 32, 16, 1024, 2);
+            const uint64_t bd = smem_desc(a + kABytes + cb * kColBBytes + kk * 32, 16, 1024, 2);
             mma_bf16_ss(d, ad, bd, idesc, (kb | k) != 0);
           }
           mma_commit(smem_u32(&sm.empty[stage]));
@@ -186,7 +203,9 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       bool ok = true;
       for (int kb = 0; kb < nk; ++kb) {
         if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteEpiFull)) { ok = false; break; }
-        const uint8_t *row = sm.stage[stage] + r * 128;
+#pragma unroll
+        for (int cb = 0; cb < kColBoxes; ++cb) {
+        const uint8_t *row = sm.stage[stage] + cb * kColABytes + r * 128;
 #pragma unroll
         for (int i = 0; i < 8; ++i) {
           // Any order covers the row; rotating by r keeps the 8 rows of a
@@ -197,6 +216,7 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           f = bf16lo(u.y); ss = fmaf(f, f, ss); f = bf16hi(u.y); ss = fmaf(f, f, ss);
           f = bf16lo(u.z); ss = fmaf(f, f, ss); f = bf16hi(u.z); ss = fmaf(f, f, ss);
           f = bf16lo(u.w); ss = fmaf(f, f, ss); f = bf16hi(u.w); ss = fmaf(f, f, ss);
+        }
         }
         __syncwarp();
         if (lane == 0) mbar_arrive(smem_u32(&sm.empty[stage]));
@@ -341,9 +361,9 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
                      cudaStream_t s) {
   using namespace k1tc;
   CUtensorMap mx, mw;
-  if (!make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, kBK, kBoxRows,
+  if (!make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBoxRows,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
-      !make_map(&mw, W, uint64_t(nC), kND, uint64_t(nC) * 2, kBK, kND,
+      !make_map(&mw, W, uint64_t(nC), kND, uint64_t(nC) * 2, 64, kND,
                 CU_TENSOR_MAP_SWIZZLE_128B)) {
     snprintf(g_msg, sizeof(g_msg), "cuTensorMapEncodeTiled failed");
     return 5;

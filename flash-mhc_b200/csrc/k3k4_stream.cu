@@ -16,13 +16,40 @@
 #include "fmhc_common.cuh"
 #include "fmhc_launch.h"
 
+// Chunks per lane in flight (U) and minimum resident blocks per SM (MINB,
+// bounds registers) of each kernel; chosen by measurement at T=65536, C=1024.
+#ifndef FMHC_K3F_U
+#define FMHC_K3F_U 2
+#endif
+#ifndef FMHC_K3F_MINB
+#define FMHC_K3F_MINB 1
+#endif
+#ifndef FMHC_K3B_U
+#define FMHC_K3B_U 2
+#endif
+#ifndef FMHC_K3B_MINB
+#define FMHC_K3B_MINB 1
+#endif
+#ifndef FMHC_K4F_U
+#define FMHC_K4F_U 2
+#endif
+#ifndef FMHC_K4F_MINB
+#define FMHC_K4F_MINB 1
+#endif
+#ifndef FMHC_K4B_U
+#define FMHC_K4B_U 1
+#endif
+#ifndef FMHC_K4B_MINB
+#define FMHC_K4B_MINB 2
+#endif
+
 namespace fmhc {
 
 using bf16 = __nv_bfloat16;
 
 // ---------------------------------------------------------------- K3 forward
-template <int VEC, int U>
-__global__ void __launch_bounds__(256)
+template <int VEC, int U, int MINB>
+__global__ void __launch_bounds__(256, MINB)
 k3_fwd_kernel(const bf16 *__restrict__ x, const float4 *__restrict__ hp,
               bf16 *__restrict__ out, int64_t T, int C) {
   const int lane = threadIdx.x & 31;
@@ -64,8 +91,8 @@ k3_fwd_kernel(const bf16 *__restrict__ x, const float4 *__restrict__ hp,
 }
 
 // --------------------------------------------------------------- K3 backward
-template <int VEC, int U>
-__global__ void __launch_bounds__(256)
+template <int VEC, int U, int MINB>
+__global__ void __launch_bounds__(256, MINB)
 k3_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const float4 *__restrict__ hp, bf16 *__restrict__ gx,
               float *__restrict__ gh, int64_t T, int C) {
@@ -117,8 +144,8 @@ k3_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
 }
 
 // ---------------------------------------------------------------- K4 forward
-template <int VEC, int U>
-__global__ void __launch_bounds__(256)
+template <int VEC, int U, int MINB>
+__global__ void __launch_bounds__(256, MINB)
 k4_fwd_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ lo,
               const float4 *__restrict__ H, const float4 *__restrict__ hpost,
               bf16 *__restrict__ out, int64_t T, int C) {
@@ -178,8 +205,8 @@ k4_fwd_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ lo,
 }
 
 // --------------------------------------------------------------- K4 backward
-template <int VEC, int U>
-__global__ void __launch_bounds__(256)
+template <int VEC, int U, int MINB>
+__global__ void __launch_bounds__(256, MINB)
 k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const bf16 *__restrict__ lo, const float4 *__restrict__ H,
               const float4 *__restrict__ hpost, bf16 *__restrict__ gx,
@@ -306,7 +333,7 @@ constexpr int kThreads = 256;
 void launch_k3_fwd(const void *x, const float *hp, void *out, int64_t T, int C, int vec,
                    cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
-    auto k = k3_fwd_kernel<VEC, 2>;
+    auto k = k3_fwd_kernel<VEC, FMHC_K3F_U, FMHC_K3F_MINB>;
     k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
         (const bf16 *)x, (const float4 *)hp, (bf16 *)out, T, C);
   });
@@ -315,7 +342,7 @@ void launch_k3_fwd(const void *x, const float *hp, void *out, int64_t T, int C, 
 void launch_k3_bwd(const void *go, const void *x, const float *hp, void *gx, float *gh,
                    int64_t T, int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
-    auto k = k3_bwd_kernel<VEC, 2>;
+    auto k = k3_bwd_kernel<VEC, FMHC_K3B_U, FMHC_K3B_MINB>;
     k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
         (const bf16 *)go, (const bf16 *)x, (const float4 *)hp, (bf16 *)gx, gh, T, C);
   });
@@ -324,7 +351,7 @@ void launch_k3_bwd(const void *go, const void *x, const float *hp, void *gx, flo
 void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *hp, void *out,
                    int64_t T, int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
-    auto k = k4_fwd_kernel<VEC, 2>;
+    auto k = k4_fwd_kernel<VEC, FMHC_K4F_U, FMHC_K4F_MINB>;
     k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
         (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)out,
         T, C);
@@ -335,7 +362,7 @@ void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H
                    const float *hp, void *gx, void *glo, float *gH, float *ghp, int64_t T,
                    int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
-    auto k = k4_bwd_kernel<VEC, 2>;
+    auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB>;
     k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
         (const bf16 *)go, (const bf16 *)x, (const bf16 *)lo, (const float4 *)H,
         (const float4 *)hp, (bf16 *)gx, (bf16 *)glo, gH, ghp, T, C);
