@@ -290,6 +290,11 @@ def run_ours(args):
 
     # --- end-to-end from host buffers --------------------------------------
     e2e = run_e2e(args, hp, one_step, torch, dist, world, dev)
+    del hp
+    torch.cuda.empty_cache()
+
+    # --- the whole block ------------------------------
+    block = None if args.no_block else run_block(args, torch, dist, world, dev)
 
     if rank == 0:
         peaks = measured_peaks()
@@ -323,6 +328,7 @@ def run_ours(args):
             "hot_path_hbm_frac": round(sum_bytes / (sum_ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4),
             "kernels": kernels,
             "e2e": e2e,
+            "block": block,
             "gpu_launches": HotPath.LAUNCHES_PER_STEP * args.steps,
             "clocks": clk.summary(),
             "native_lib": os.path.relpath(lib_path, ROOT),
@@ -344,6 +350,61 @@ def _physical_gpu_indices(world):
         except ValueError:
             pass
     return list(range(world))
+
+
+def run_block(args, torch, dist, world, dev):
+    """MHCLiteBlock fwd+bwd with activation checkpointing:
+    T tokens per GPU, C=2048, n=4 bf16, wrapped nn.Linear(C, C, bias=False)
+    ~N(0,0.02), upstream grad ~N(0,1); with N GPUs the block's parameter
+    gradients are all-reduced (one bucket) every step."""
+    import torch.nn as nn
+
+    from flash_mhc import MHCLiteBlock
+    from flash_mhc.distributed import allreduce_gradients
+
+    T, C = args.block_T, args.block_C
+    g = torch.Generator(device=dev)
+    g.manual_seed(77)
+    layer = nn.Linear(C, C, bias=False)
+    blk = MHCLiteBlock(4, C, layer, triton_fused=True, activation_checkpointing=True)
+    blk = blk.to(dev).to(torch.bfloat16).train()
+    with torch.no_grad():
+        layer.weight.copy_((torch.randn(C, C, generator=g, device=dev) * 0.02).bfloat16())
+    x = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16().requires_grad_(True)
+    up = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16()
+
+    def step():
+        blk.zero_grad(set_to_none=True)
+        x.grad = None
+        out = blk(x)
+        out.backward(up)
+        if world > 1:
+            allreduce_gradients(blk)
+
+    steps = max(1, min(args.steps, 10))
+    for _ in range(max(3, min(args.warmup, 5))):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    flops = 3 * 2 * T * C * C  # the wrapped layer's fwd + 2 bwd GEMMs
+    return {"config": {"workload": "MHCLiteBlock fwd+bwd, activation checkpointing (configs[2])",
+                       "T_per_gpu": T, "C": C, "n": N_STREAMS,
+                       "layer": "nn.Linear(C, C, bias=False) ~N(0,0.02)"},
+            "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT, "ms_per_step": round(ms, 4),
+            "steps": steps, "layer_gemm_tflops_per_step": round(flops / 1e12, 3)}
 
 
 def run_e2e(args, hp, one_step, torch, dist, world, dev):
@@ -497,6 +558,9 @@ def main():
     ap.add_argument("--cpu-tokens-per-worker", type=int, default=1024)
     ap.add_argument("--cpu-reps", type=int, default=4)
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--no-block", action="store_true", help="skip the MHCLiteBlock measurement")
+    ap.add_argument("--block-T", type=int, default=65536, help="tokens per GPU for the block")
+    ap.add_argument("--block-C", type=int, default=2048)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: the timing rules ask for >= 3 warm-up steps", file=sys.stderr)

@@ -101,11 +101,29 @@ int fmhc_k3_bwd(const void *grad_out, const void *x, const float *h_pre, void *g
   if (int e = check_streams(w, T, n, C)) return e;
   if (T == 0) return ok();
   FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, h_pre);
-  FMHC_REQUIRE_PTR(w, grad_x); FMHC_REQUIRE_PTR(w, grad_h);
+  FMHC_REQUIRE_PTR(w, grad_h);
   FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, grad_h);
-  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, grad_x);
-  const int vec = pick_vec(C, {grad_out, x, grad_x});
+  FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x);
+  if (grad_x) FMHC_REQUIRE_ALIGN2(w, grad_x);
+  const int vec = grad_x ? pick_vec(C, {grad_out, x, grad_x}) : pick_vec(C, {grad_out, x});
   fmhc::launch_k3_bwd(grad_out, x, h_pre, grad_x, grad_h, T, int(C), vec, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int fmhc_mhc_grad_x_combine(const void *gx1, const void *grad_li, const float *h_pre,
+                            const void *gx4, void *grad_x, int64_t T, int64_t n, int64_t C,
+                            void *stream) {
+  const char *w = "fmhc_mhc_grad_x_combine";
+  if (int e = check_streams(w, T, n, C)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, gx1); FMHC_REQUIRE_PTR(w, grad_li); FMHC_REQUIRE_PTR(w, h_pre);
+  FMHC_REQUIRE_PTR(w, grad_x);
+  FMHC_REQUIRE_ALIGN16(w, h_pre);
+  FMHC_REQUIRE_ALIGN2(w, gx1); FMHC_REQUIRE_ALIGN2(w, grad_li); FMHC_REQUIRE_ALIGN2(w, grad_x);
+  if (gx4) FMHC_REQUIRE_ALIGN2(w, gx4);
+  const int vec = gx4 ? pick_vec(C, {gx1, grad_li, gx4, grad_x}) : pick_vec(C, {gx1, grad_li, grad_x});
+  fmhc::launch_grad_x_combine(gx1, grad_li, h_pre, gx4, grad_x, T, int(C), vec,
+                              (cudaStream_t)stream);
   return check_launch(w);
 }
 
@@ -238,6 +256,56 @@ int fmhc_k1_bwd(const void *grad_out, const void *x, const void *W, const void *
     fmhc::launch_k1_dw_simt(grad_out, x, inv_rms, grad_W, (float *)workspace, T, int(nC),
                             int(D), s);
   }
+  return check_launch(w);
+}
+
+int fmhc_k2_fwd(const void *proj, const float *params, const float *perm, float *h_pre,
+                float *h_post, float *H_merged, int64_t T, void *stream) {
+  const char *w = "fmhc_k2_fwd";
+  if (T < 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: T must be >= 0 (got %lld)", w, (long long)T);
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, params); FMHC_REQUIRE_PTR(w, perm);
+  FMHC_REQUIRE_PTR(w, h_pre); FMHC_REQUIRE_PTR(w, h_post); FMHC_REQUIRE_PTR(w, H_merged);
+  FMHC_REQUIRE_ALIGN16(w, proj); FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, h_post);
+  FMHC_REQUIRE_ALIGN16(w, H_merged);
+  if (!aligned(params, 4) || !aligned(perm, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: params/perm must be 4-byte aligned", w);
+  fmhc::launch_k2_fwd(proj, params, perm, h_pre, h_post, H_merged, T, (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int64_t fmhc_k2_bwd_workspace_size(int64_t T) {
+  if (T <= 0) return 0;
+  return fmhc::k2_bwd_workspace_bytes(T);
+}
+
+int fmhc_k2_bwd(const void *proj, const float *params, const float *perm, const float *grad_h_pre,
+                const float *grad_h_post, const float *grad_H_merged, void *grad_proj,
+                float *grad_params, void *workspace, int64_t workspace_bytes, int64_t T,
+                void *stream) {
+  const char *w = "fmhc_k2_bwd";
+  if (T < 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: T must be >= 0 (got %lld)", w, (long long)T);
+  FMHC_REQUIRE_PTR(w, grad_params);
+  cudaStream_t s = (cudaStream_t)stream;
+  if (T == 0) {
+    if (cudaMemsetAsync(grad_params, 0, 35 * sizeof(float), s) != cudaSuccess)
+      return fail(FMHC_ERR_CUDA, "%s: cudaMemsetAsync failed", w);
+    return ok();
+  }
+  FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, params); FMHC_REQUIRE_PTR(w, perm);
+  FMHC_REQUIRE_PTR(w, grad_h_pre); FMHC_REQUIRE_PTR(w, grad_h_post);
+  FMHC_REQUIRE_PTR(w, grad_H_merged); FMHC_REQUIRE_PTR(w, grad_proj); FMHC_REQUIRE_PTR(w, workspace);
+  FMHC_REQUIRE_ALIGN16(w, proj); FMHC_REQUIRE_ALIGN16(w, grad_h_pre);
+  FMHC_REQUIRE_ALIGN16(w, grad_h_post); FMHC_REQUIRE_ALIGN16(w, grad_H_merged);
+  FMHC_REQUIRE_ALIGN16(w, grad_proj);
+  if (!aligned(workspace, 256)) return fail(FMHC_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", w);
+  if (!aligned(params, 4) || !aligned(perm, 4) || !aligned(grad_params, 4))
+    return fail(FMHC_ERR_ALIGNMENT, "%s: params/perm/grad_params must be 4-byte aligned", w);
+  const int64_t need = fmhc::k2_bwd_workspace_bytes(T);
+  if (workspace_bytes < need)
+    return fail(FMHC_ERR_WORKSPACE, "%s: workspace of %lld bytes, %lld needed", w,
+                (long long)workspace_bytes, (long long)need);
+  fmhc::launch_k2_bwd(proj, params, perm, grad_h_pre, grad_h_post, grad_H_merged, grad_proj,
+                      grad_params, (float *)workspace, T, s);
   return check_launch(w);
 }
 

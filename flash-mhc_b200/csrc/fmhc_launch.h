@@ -17,6 +17,8 @@ void launch_k3_bwd(const void *go, const void *x, const float *hp, void *gx, flo
                    int64_t T, int C, int vec, cudaStream_t s);
 void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *hp, void *out,
                    int64_t T, int C, int vec, cudaStream_t s);
+void launch_grad_x_combine(const void *gx1, const void *gli, const float *hp, const void *gx4,
+                           void *gx, int64_t T, int C, int vec, cudaStream_t s);
 void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H,
                    const float *hp, void *gx, void *glo, float *gH, float *ghp, int64_t T,
                    int C, int vec, cudaStream_t s);
@@ -31,5 +33,13 @@ int k1_dw_splits(int64_t T);
 int64_t k1_dw_workspace_bytes(int64_t T, int64_t nC, int64_t D);
 void launch_k1_dw_simt(const void *go, const void *x, const float *inv_rms, void *gW,
                        float *ws, int64_t T, int nC, int D, cudaStream_t s);
+
+// k2_coeffs.cu -- coefficient math (n = 4, D = 32).
+int64_t k2_bwd_workspace_bytes(int64_t T);
+void launch_k2_fwd(const void *proj, const float *params, const float *perm, float *h_pre,
+                   float *h_post, float *H, int64_t T, cudaStream_t s);
+void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
+                   const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
+                   float *ws, int64_t T, cudaStream_t s);
 
 }  // namespace fmhc

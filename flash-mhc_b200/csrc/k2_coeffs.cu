@@ -1,0 +1,251 @@
+// K2: the per-token coefficient math of mHC-lite, forward and backward, as one
+// kernel each (the reference runs it as ~20 eager torch launches in the
+// caller, src/flash_mhc/block.py:150-170).
+//
+// Per token, from the 32 projection logits proj = [p (4) | q (4) | r (24)]:
+//   h_pre   = sigmoid(a_pre * p + b[0:4])
+//   h_post  = 2 * sigmoid(a_post * q + b[4:8])
+//   a       = softmax(a_res * r + b[8:32])              (over the 24 entries)
+//   H_res   = sum_k a[k] * perm[k]                      (4x4, perm rows are the
+//                                                        flattened permutation matrices)
+//   H_merged= H_res - h_post (outer) h_pre
+// The reference evaluates this in the input dtype (bf16): alphas and bias are
+// cast to bf16 and h_pre, h_post, H_merged are stored as bf16 before the
+// f32 copies that K3/K4 consume.  Here the parameters are rounded to bf16 the
+// same way and the three outputs are rounded to bf16 (then stored as f32),
+// while the intermediate arithmetic runs in f32 (the reference rounds every
+// intermediate op to bf16; the results agree to bf16 rounding).
+//
+// The backward takes the f32 gradients of h_pre (from K3's backward), h_post
+// and H_merged (from K4's backward), recomputes the forward intermediates from
+// proj and returns grad_proj (bf16, the dtype of proj) plus the parameter
+// gradients (3 alphas, 32 bias entries) summed over tokens in a fixed order.
+#include "fmhc_common.cuh"
+#include "fmhc_launch.h"
+
+namespace fmhc {
+
+using bf16 = __nv_bfloat16;
+
+namespace {
+
+constexpr int kP = 35;  // a_pre, a_post, a_res, bias[32]
+constexpr int kNF = 24; // permutations of 4
+
+__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
+__device__ __forceinline__ float sigm(float z) { return 1.f / (1.f + __expf(-z)); }
+
+struct K2Smem {
+  float par[kP];
+  float perm[kNF * 16];
+};
+
+__device__ __forceinline__ void load_params(K2Smem &sm, const float *params, const float *perm) {
+  for (int i = threadIdx.x; i < kP; i += blockDim.x) sm.par[i] = bf16r(params[i]);
+  for (int i = threadIdx.x; i < kNF * 16; i += blockDim.x) sm.perm[i] = bf16r(perm[i]);
+  __syncthreads();
+}
+
+__device__ __forceinline__ void load_proj(const bf16 *proj, int64_t t, float (&v)[32]) {
+  const uint4 *p4 = reinterpret_cast<const uint4 *>(proj + t * 32);
+#pragma unroll
+  for (int c = 0; c < 4; ++c) {
+    const uint4 u = __ldg(p4 + c);
+    v[8 * c + 0] = bf16lo(u.x); v[8 * c + 1] = bf16hi(u.x);
+    v[8 * c + 2] = bf16lo(u.y); v[8 * c + 3] = bf16hi(u.y);
+    v[8 * c + 4] = bf16lo(u.z); v[8 * c + 5] = bf16hi(u.z);
+    v[8 * c + 6] = bf16lo(u.w); v[8 * c + 7] = bf16hi(u.w);
+  }
+}
+
+// Forward intermediates of one token.
+struct K2Tok {
+  float spre[4], spost[4];  // sigmoids (unrounded)
+  float hpre[4], hpost[4];  // bf16-rounded outputs
+  float a[kNF];             // softmax
+};
+
+__device__ __forceinline__ void k2_forward_token(const K2Smem &sm, const float (&v)[32], K2Tok &k) {
+  const float ap = sm.par[0], aq = sm.par[1], ar = sm.par[2];
+  const float *b = sm.par + 3;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    k.spre[i] = sigm(ap * v[i] + b[i]);
+    k.hpre[i] = bf16r(k.spre[i]);
+    k.spost[i] = sigm(aq * v[4 + i] + b[4 + i]);
+    k.hpost[i] = bf16r(2.f * k.spost[i]);
+  }
+  float m = -INFINITY;
+#pragma unroll
+  for (int j = 0; j < kNF; ++j) {
+    k.a[j] = ar * v[8 + j] + b[8 + j];
+    m = fmaxf(m, k.a[j]);
+  }
+  float s = 0.f;
+#pragma unroll
+  for (int j = 0; j < kNF; ++j) {
+    k.a[j] = __expf(k.a[j] - m);
+    s += k.a[j];
+  }
+  const float inv = 1.f / s;
+#pragma unroll
+  for (int j = 0; j < kNF; ++j) k.a[j] *= inv;
+}
+
+}  // namespace
+
+__global__ void __launch_bounds__(256)
+k2_fwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
+              const float *__restrict__ perm, float4 *__restrict__ h_pre,
+              float4 *__restrict__ h_post, float4 *__restrict__ H, int64_t T) {
+  __shared__ K2Smem sm;
+  load_params(sm, params, perm);
+  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (t >= T) return;
+  float v[32];
+  load_proj(proj, t, v);
+  K2Tok k;
+  k2_forward_token(sm, v, k);
+  float Hm[16];
+#pragma unroll
+  for (int e = 0; e < 16; ++e) {
+    float acc = 0.f;  // bf16 softmax output times the bf16 permutation rows, f32 accumulate
+#pragma unroll
+    for (int j = 0; j < kNF; ++j) acc = fmaf(bf16r(k.a[j]), sm.perm[j * 16 + e], acc);
+    Hm[e] = bf16r(bf16r(acc) - bf16r(k.hpost[e >> 2] * k.hpre[e & 3]));
+  }
+  h_pre[t] = make_float4(k.hpre[0], k.hpre[1], k.hpre[2], k.hpre[3]);
+  h_post[t] = make_float4(k.hpost[0], k.hpost[1], k.hpost[2], k.hpost[3]);
+#pragma unroll
+  for (int i = 0; i < 4; ++i)
+    H[t * 4 + i] = make_float4(Hm[4 * i + 0], Hm[4 * i + 1], Hm[4 * i + 2], Hm[4 * i + 3]);
+}
+
+// One thread per token; each block writes the sums of its tokens' parameter
+// gradients to part[blockIdx.x][35].
+__global__ void __launch_bounds__(256)
+k2_bwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
+              const float *__restrict__ perm, const float4 *__restrict__ g_hpre,
+              const float4 *__restrict__ g_hpost, const float4 *__restrict__ g_H,
+              bf16 *__restrict__ g_proj, float *__restrict__ part, int64_t T) {
+  __shared__ K2Smem sm;
+  __shared__ float red[8][kP];
+  load_params(sm, params, perm);
+  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  float gp[kP];  // this token's contribution to the 35 parameter gradients
+#pragma unroll
+  for (int i = 0; i < kP; ++i) gp[i] = 0.f;
+  if (t < T) {
+    float v[32];
+    load_proj(proj, t, v);
+    K2Tok k;
+    k2_forward_token(sm, v, k);
+    const float4 a4 = g_hpre[t], b4 = g_hpost[t];
+    float ghpre[4] = {a4.x, a4.y, a4.z, a4.w};
+    float ghpost[4] = {b4.x, b4.y, b4.z, b4.w};
+    float gH[16];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float4 r = g_H[t * 4 + i];
+      gH[4 * i + 0] = r.x; gH[4 * i + 1] = r.y; gH[4 * i + 2] = r.z; gH[4 * i + 3] = r.w;
+    }
+    // H_merged = H_res - h_post (outer) h_pre
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+#pragma unroll
+      for (int j = 0; j < 4; ++j) {
+        ghpost[i] = fmaf(-gH[4 * i + j], k.hpre[j], ghpost[i]);
+        ghpre[j] = fmaf(-gH[4 * i + j], k.hpost[i], ghpre[j]);
+      }
+    }
+    // H_res = sum_k a_k perm_k ; softmax backward
+    float ga[kNF], dot = 0.f;
+#pragma unroll
+    for (int j = 0; j < kNF; ++j) {
+      float acc = 0.f;
+#pragma unroll
+      for (int e = 0; e < 16; ++e) acc = fmaf(gH[e], sm.perm[j * 16 + e], acc);
+      ga[j] = acc;
+      dot = fmaf(acc, k.a[j], dot);
+    }
+    const float ap = sm.par[0], aq = sm.par[1], ar = sm.par[2];
+    float g[32];
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+      const float zpre = ghpre[i] * k.spre[i] * (1.f - k.spre[i]);
+      const float zpost = ghpost[i] * 2.f * k.spost[i] * (1.f - k.spost[i]);
+      g[i] = zpre * ap;
+      g[4 + i] = zpost * aq;
+      gp[0] = fmaf(zpre, v[i], gp[0]);
+      gp[1] = fmaf(zpost, v[4 + i], gp[1]);
+      gp[3 + i] = zpre;
+      gp[7 + i] = zpost;
+    }
+#pragma unroll
+    for (int j = 0; j < kNF; ++j) {
+      const float zr = k.a[j] * (ga[j] - dot);
+      g[8 + j] = zr * ar;
+      gp[2] = fmaf(zr, v[8 + j], gp[2]);
+      gp[11 + j] = zr;
+    }
+    uint4 *o = reinterpret_cast<uint4 *>(g_proj + t * 32);
+#pragma unroll
+    for (int c = 0; c < 4; ++c) {
+      uint4 w;
+      w.x = pack_bf16x2(g[8 * c + 0], g[8 * c + 1]);
+      w.y = pack_bf16x2(g[8 * c + 2], g[8 * c + 3]);
+      w.z = pack_bf16x2(g[8 * c + 4], g[8 * c + 5]);
+      w.w = pack_bf16x2(g[8 * c + 6], g[8 * c + 7]);
+      o[c] = w;
+    }
+  }
+  // Block sum of the 35 parameter gradients: warp butterflies, then the 8
+  // warp sums in warp order.
+  const int lane = threadIdx.x & 31, warp = threadIdx.x >> 5;
+#pragma unroll
+  for (int i = 0; i < kP; ++i) {
+    float s = gp[i];
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+    if (lane == 0) red[warp][i] = s;
+  }
+  __syncthreads();
+  if (threadIdx.x < kP) {
+    float s = 0.f;
+    for (int w = 0; w < int(blockDim.x >> 5); ++w) s += red[w][threadIdx.x];
+    part[int64_t(blockIdx.x) * kP + threadIdx.x] = s;
+  }
+}
+
+__global__ void k2_param_reduce_kernel(const float *__restrict__ part, float *__restrict__ g_params,
+                                       int nblocks) {
+  const int i = threadIdx.x;
+  if (i >= kP) return;
+  float s = 0.f;
+  for (int b = 0; b < nblocks; ++b) s += part[int64_t(b) * kP + i];
+  g_params[i] = s;
+}
+
+int64_t k2_bwd_workspace_bytes(int64_t T) {
+  const int64_t nb = (T + 255) / 256;
+  return ((nb * kP * 4) + 255) & ~int64_t(255);
+}
+
+void launch_k2_fwd(const void *proj, const float *params, const float *perm, float *h_pre,
+                   float *h_post, float *H, int64_t T, cudaStream_t s) {
+  const unsigned nb = unsigned((T + 255) / 256);
+  k2_fwd_kernel<<<nb, 256, 0, s>>>((const bf16 *)proj, params, perm, (float4 *)h_pre,
+                                   (float4 *)h_post, (float4 *)H, T);
+}
+
+void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
+                   const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
+                   float *ws, int64_t T, cudaStream_t s) {
+  const unsigned nb = unsigned((T + 255) / 256);
+  k2_bwd_kernel<<<nb, 256, 0, s>>>((const bf16 *)proj, params, perm, (const float4 *)g_hpre,
+                                   (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj,
+                                   ws, T);
+  k2_param_reduce_kernel<<<1, 64, 0, s>>>(ws, g_params, int(nb));
+}
+
+}  // namespace fmhc

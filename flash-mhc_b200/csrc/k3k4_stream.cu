@@ -133,7 +133,7 @@ k3_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               o[e] = hj[j] * fg[e];
               acc[j] = fmaf(fx[e], fg[e], acc[j]);
             }
-            store_stream<VEC>(gxr + j * C + c * VEC, o);
+            if (gx) store_stream<VEC>(gxr + j * C + c * VEC, o);
           }
         }
       }
@@ -295,6 +295,64 @@ k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
   }
 }
 
+// ------------------------------------------ combined grad_x of the block
+// gx[t,j,c] = bf16( gx1[t,j,c] + h_pre[t,j] * g_li[t,c] + gx4[t,j,c] )
+// The three contributions to the gradient of the residual streams (K1's
+// backward, K3's grad_x, K4's grad_x) in one pass; gx4 may be null.
+template <int VEC, int U>
+__global__ void __launch_bounds__(256)
+grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli,
+                      const float4 *__restrict__ hp, const bf16 *__restrict__ gx4,
+                      bf16 *__restrict__ gx, int64_t T, int C) {
+  const int lane = threadIdx.x & 31;
+  const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
+  const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
+  const int nchunk = C / VEC;
+  for (int64_t t = warp; t < T; t += nwarps) {
+    const float4 h = __ldg(hp + t);
+    const float hj[4] = {h.x, h.y, h.z, h.w};
+    const int64_t row = t * 4 * C;
+    for (int c0 = lane; c0 < nchunk; c0 += 32 * U) {
+      Chunk<VEC> g[U], a[U][4], b[U][4];
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + 32 * u;
+        if (c < nchunk) {
+          g[u] = ld_raw<VEC>(gli + t * C + c * VEC);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            a[u][j] = ld_raw<VEC>(gx1 + row + j * C + c * VEC);
+            if (gx4) b[u][j] = ld_raw<VEC>(gx4 + row + j * C + c * VEC);
+          }
+        }
+      }
+#pragma unroll
+      for (int u = 0; u < U; ++u) {
+        const int c = c0 + 32 * u;
+        if (c < nchunk) {
+          float fg[VEC];
+          unpack(g[u], fg);
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            float fa[VEC], o[VEC];
+            unpack(a[u][j], fa);
+            if (gx4) {
+              float fb[VEC];
+              unpack(b[u][j], fb);
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) o[e] = fmaf(hj[j], fg[e], fa[e] + fb[e]);
+            } else {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) o[e] = fmaf(hj[j], fg[e], fa[e]);
+            }
+            store_stream<VEC>(gx + row + j * C + c * VEC, o);
+          }
+        }
+      }
+    }
+  }
+}
+
 // ------------------------------------------------------------------ launchers
 namespace {
 
@@ -354,6 +412,16 @@ void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *h
     auto k = k4_fwd_kernel<VEC, FMHC_K4F_U, FMHC_K4F_MINB>;
     k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
         (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)out,
+        T, C);
+  });
+}
+
+void launch_grad_x_combine(const void *gx1, const void *gli, const float *hp, const void *gx4,
+                           void *gx, int64_t T, int C, int vec, cudaStream_t s) {
+  FMHC_DISPATCH_VEC(vec, {
+    auto k = grad_x_combine_kernel<VEC, 2>;
+    k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
+        (const bf16 *)gx1, (const bf16 *)gli, (const float4 *)hp, (const bf16 *)gx4, (bf16 *)gx,
         T, C);
   });
 }

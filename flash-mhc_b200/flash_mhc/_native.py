@@ -31,8 +31,12 @@ _SIGNATURES = {
     "fmhc_k1_bwd_dx": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k1_bwd_workspace_size": [_i64, _i64, _i64],
     "fmhc_k1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],
+    "fmhc_k2_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _vp],
+    "fmhc_k2_bwd_workspace_size": [_i64],
+    "fmhc_k2_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "fmhc_k3_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k3_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "fmhc_mhc_grad_x_combine": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k4_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k4_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
 }
@@ -40,6 +44,7 @@ _RESTYPES = {
     "fmhc_last_error": ctypes.c_char_p,
     "fmhc_version": ctypes.c_char_p,
     "fmhc_k1_bwd_workspace_size": _i64,
+    "fmhc_k2_bwd_workspace_size": _i64,
 }
 
 STATUS = {

@@ -10,11 +10,19 @@ doubly-stochastic H_res (n x n) built as a convex combination of the n!
 permutation matrices, (K3) pre-mixes the streams into the wrapped layer's
 input, runs the layer, and (K4) post-mixes H_merged @ x + h_post * layer_out.
 
-The fused path (CUDA + bfloat16 + (T, n, C) + n == 4) runs K1, K3 and K4 as
-the sm_100a kernels behind ``torch.ops.flash_mhc``; K2 stays in eager torch in
-the input dtype, as in the reference.  Every other input takes the
-pure-PyTorch path (which is also what runs on CPU).  The constructor argument
-keeps its reference name ``triton_fused``; here it selects the CUDA kernels.
+The fused path (CUDA + bfloat16 + (T, n, C) + n == 4) runs K1, K2, K3 and K4
+as sm_100a kernels behind ``torch.ops.flash_mhc`` inside two autograd
+functions that save only what the backward kernels read (x, the layer output,
+the 32 projection logits, inv_rms and the f32 coefficients: ~170 bytes per
+token besides x and the layer output) and recompute nothing.  Activation
+checkpointing is therefore unnecessary on this path: with
+``activation_checkpointing=True`` the reference re-runs K1, K2, K3 and K4 in
+the backward to avoid storing layer_input and the block output; the fused path
+never stores those either, so the flag leaves its memory and results unchanged
+and skips the recomputation.  Every other input takes the pure-PyTorch path
+(which is also what runs on CPU), with the flag honoured through torch
+checkpointing exactly as in the reference.  The constructor argument keeps its
+reference name ``triton_fused``; here it selects the CUDA kernels.
 """
 
 from __future__ import annotations
@@ -28,6 +36,81 @@ import torch.nn.functional as F
 from torch.utils.checkpoint import checkpoint as _checkpoint
 
 from . import ops as _ops  # noqa: F401  (registers torch.ops.flash_mhc.*)
+
+
+class _StreamGrad:
+    """Hands K4's grad_x from the post-res backward to the pre-map backward.
+
+    The post-res backward always runs first (the pre-map's outputs feed it),
+    so instead of returning its grad_x to the autograd engine, which would add
+    it to the pre-map's grad_x with a separate full pass, it parks the tensor
+    here and the pre-map backward folds it into its one combining pass.
+    """
+
+    __slots__ = ("gx4",)
+
+    def __init__(self):
+        self.gx4 = None
+
+
+class _FusedPreMap(torch.autograd.Function):
+    """K1 (RMSNorm + projection), K2 (coefficients), K3 (pre-map) forward.
+
+    Backward from saved tensors only (no forward kernel is re-run):
+    K3's grad_h_pre -> K2 bwd -> K1 bwd (grad_x and grad_W in one pass), then
+    one pass forming grad_x = K1's + h_pre * grad_layer_input + K4's.
+    """
+
+    @staticmethod
+    def forward(ctx, x, W, a_pre, a_post, a_res, bias, perm, slot):
+        ops = torch.ops.flash_mhc
+        T, n, C = x.shape
+        proj, inv = ops.fused_rmsnorm_project(x.reshape(T, n * C), W)
+        h_pre, h_post, H = ops.mhc_coeffs(proj, a_pre, a_post, a_res, bias, perm)
+        layer_input = ops.fused_pre_map(x, h_pre)
+        ctx.save_for_backward(x, W, proj, inv, h_pre, a_pre, a_post, a_res, bias, perm)
+        ctx.slot = slot
+        return layer_input, H, h_post
+
+    @staticmethod
+    def backward(ctx, g_li, g_H, g_hpost):
+        ops = torch.ops.flash_mhc
+        x, W, proj, inv, h_pre, a_pre, a_post, a_res, bias, perm = ctx.saved_tensors
+        T, n, C = x.shape
+        z = lambda *s: torch.zeros(*s, device=x.device, dtype=torch.float32)  # noqa: E731
+        if g_li is None:
+            g_li = torch.zeros((T, C), device=x.device, dtype=x.dtype)
+        g_hpre = ops.pre_map_grad_h(g_li, x, h_pre)
+        g_proj, gp = ops.mhc_coeffs_backward(
+            g_hpre, z(T, 4) if g_hpost is None else g_hpost, z(T, 4, 4) if g_H is None else g_H,
+            proj, a_pre, a_post, a_res, bias, perm)
+        gx1, gW = ops.fused_rmsnorm_project_backward(g_proj, x.reshape(T, n * C), W, proj, inv)
+        gx4, ctx.slot.gx4 = ctx.slot.gx4, None
+        gx = ops.mhc_grad_x_combine(gx1.view(T, n, C), g_li, h_pre, gx4)
+        return (gx, gW, gp[0:1].view_as(a_pre).to(a_pre.dtype),
+                gp[1:2].view_as(a_post).to(a_post.dtype), gp[2:3].view_as(a_res).to(a_res.dtype),
+                gp[3:35].view_as(bias).to(bias.dtype), None, None)
+
+
+class _FusedPostRes(torch.autograd.Function):
+    """K4 forward; backward K4 bwd from the saved inputs (the output is not kept).
+
+    K4's grad_x goes to the pre-map backward through ``slot`` (see _StreamGrad);
+    the engine receives None for x from here.
+    """
+
+    @staticmethod
+    def forward(ctx, x, layer_output, H_merged, h_post, slot):
+        ctx.save_for_backward(x, layer_output, H_merged, h_post)
+        ctx.slot = slot
+        return torch.ops.flash_mhc.fused_post_res(x, layer_output, H_merged, h_post)
+
+    @staticmethod
+    def backward(ctx, g_out):
+        x, lo, H, hp = ctx.saved_tensors
+        gx4, glo, gH, ghp = torch.ops.flash_mhc.fused_post_res_backward(g_out, x, lo, H, hp)
+        ctx.slot.gx4 = gx4
+        return None, glo, gH, ghp, None
 
 
 def build_permutation_matrices(n: int) -> tuple[torch.Tensor, int]:
@@ -137,24 +220,33 @@ class MHCLiteBlock(nn.Module):
 
     # ------------------------------------------------------------- fused
     def _mhc_coeffs_triton(self, x_streams: torch.Tensor):
+        """K1 + K2 through the ops (f32 coefficients, rounded to bf16 like the reference)."""
         dt = x_streams.dtype
         T = x_streams.shape[0]
         x_flat = x_streams.reshape(T, self.nC)
         all_proj, _inv_rms = torch.ops.flash_mhc.fused_rmsnorm_project(
             x_flat, self.W_all.weight.to(dt))
-        return self._coeffs_from_proj(all_proj, dt)
+        return torch.ops.flash_mhc.mhc_coeffs(all_proj, self.alpha_pre, self.alpha_post,
+                                             self.alpha_res, self.W_all.bias, self.perm_mat)
 
-    def _mhc_pre_map_triton(self, x_streams: torch.Tensor):
-        h_pre, h_post, H_merged = self._mhc_coeffs_triton(x_streams)
-        layer_input = torch.ops.flash_mhc.fused_pre_map(x_streams, h_pre.float())
-        return layer_input, H_merged.float(), h_post.float()
+    def _mhc_pre_map_triton(self, x_streams: torch.Tensor, slot=None):
+        return _FusedPreMap.apply(x_streams, self.W_all.weight.to(x_streams.dtype),
+                                  self.alpha_pre, self.alpha_post, self.alpha_res,
+                                  self.W_all.bias, self.perm_mat,
+                                  _StreamGrad() if slot is None else slot)
 
-    def _mhc_post_res_triton(self, x_streams, layer_output, H_merged, h_post):
-        return torch.ops.flash_mhc.fused_post_res(x_streams, layer_output, H_merged, h_post)
+    def _mhc_post_res_triton(self, x_streams, layer_output, H_merged, h_post, slot=None):
+        if slot is None:  # standalone use: K4's grad_x must reach the engine
+            return torch.ops.flash_mhc.fused_post_res(x_streams, layer_output, H_merged, h_post)
+        return _FusedPostRes.apply(x_streams, layer_output, H_merged, h_post, slot)
 
     def _forward_triton(self, x_streams: torch.Tensor, **kwargs) -> torch.Tensor:
-        return self._run(x_streams, self._mhc_pre_map_triton, self._mhc_post_res_triton,
-                         **kwargs)
+        # No torch checkpointing here: the fused autograd functions already keep
+        # only the small per-token tensors their backward kernels read.
+        slot = _StreamGrad()
+        layer_input, H_merged, h_post = self._mhc_pre_map_triton(x_streams, slot)
+        layer_output = self.layer(layer_input, **kwargs)
+        return self._mhc_post_res_triton(x_streams, layer_output, H_merged, h_post, slot)
 
     # The reference name is kept above; this alias says what runs.
     _forward_fused = _forward_triton

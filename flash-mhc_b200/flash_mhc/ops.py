@@ -47,6 +47,19 @@ _lib.define(
 _lib.define(
     "fused_rmsnorm_project_backward(Tensor grad_out, Tensor x_flat, Tensor W, Tensor proj_out, Tensor inv_rms) -> (Tensor grad_x, Tensor grad_W)"
 )
+# Not in the reference: K2 (the coefficient math of block.py:150-170) as one
+# kernel each way; outputs are the f32 coefficients K3/K4 consume.
+_lib.define(
+    "mhc_coeffs(Tensor proj, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor h_pre, Tensor h_post, Tensor H_merged)"
+)
+# Not in the reference: pieces of the fused block backward.
+_lib.define("pre_map_grad_h(Tensor grad_out, Tensor x_streams, Tensor h_pre) -> Tensor grad_h_pre")
+_lib.define(
+    "mhc_grad_x_combine(Tensor gx1, Tensor grad_layer_input, Tensor h_pre, Tensor? gx4) -> Tensor grad_x"
+)
+_lib.define(
+    "mhc_coeffs_backward(Tensor grad_h_pre, Tensor grad_h_post, Tensor grad_H_merged, Tensor proj, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor grad_proj, Tensor grad_params)"
+)
 
 # ---------------------------------------------------------------------------
 # Autotune controls.  The reference exposes a thread-local context manager and
@@ -100,6 +113,29 @@ def _fused_rmsnorm_project_bwd_dx_fake(grad_out, x_flat, W, proj_out, inv_rms):
 @torch.library.register_fake("flash_mhc::fused_rmsnorm_project_backward")
 def _fused_rmsnorm_project_backward_fake(grad_out, x_flat, W, proj_out, inv_rms):
     return torch.empty_like(x_flat), torch.empty_like(W, dtype=x_flat.dtype)
+
+
+@torch.library.register_fake("flash_mhc::mhc_coeffs")
+def _mhc_coeffs_fake(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
+    T = proj.shape[0]
+    f = dict(device=proj.device, dtype=torch.float32)
+    return torch.empty((T, 4), **f), torch.empty((T, 4), **f), torch.empty((T, 4, 4), **f)
+
+
+@torch.library.register_fake("flash_mhc::mhc_coeffs_backward")
+def _mhc_coeffs_backward_fake(grad_h_pre, grad_h_post, grad_H_merged, proj, alpha_pre,
+                              alpha_post, alpha_res, bias, perm):
+    return torch.empty_like(proj), torch.empty((35,), device=proj.device, dtype=torch.float32)
+
+
+@torch.library.register_fake("flash_mhc::pre_map_grad_h")
+def _pre_map_grad_h_fake(grad_out, x_streams, h_pre):
+    return torch.empty_like(h_pre, dtype=torch.float32)
+
+
+@torch.library.register_fake("flash_mhc::mhc_grad_x_combine")
+def _mhc_grad_x_combine_fake(gx1, grad_layer_input, h_pre, gx4):
+    return torch.empty_like(gx1)
 
 
 @torch.library.register_fake("flash_mhc::fused_pre_map")
@@ -228,6 +264,45 @@ def _fused_rmsnorm_project_backward_cuda(grad_out, x_flat, W, proj_out, inv_rms)
     return grad_x, grad_W
 
 
+def _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
+    if proj.dim() != 2 or proj.shape[1] != 32:
+        raise ValueError(f"flash_mhc::mhc_coeffs: proj must be (T, 32) (n=4), got {tuple(proj.shape)}")
+    if bias.numel() != 32 or perm.shape != (24, 16):
+        raise ValueError("flash_mhc::mhc_coeffs: bias must have 32 entries and perm be (24, 16)")
+    params = torch.cat([alpha_pre.reshape(-1)[:1], alpha_post.reshape(-1)[:1],
+                        alpha_res.reshape(-1)[:1], bias.reshape(-1)]).to(torch.float32).contiguous()
+    return _bf16("proj", proj), params, perm.to(torch.float32).contiguous()
+
+
+@torch.library.impl(_lib, "mhc_coeffs", "CUDA")
+def _mhc_coeffs_cuda(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
+    proj, params, perm = _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm)
+    T = proj.shape[0]
+    f = dict(device=proj.device, dtype=torch.float32)
+    h_pre, h_post, H = torch.empty((T, 4), **f), torch.empty((T, 4), **f), torch.empty((T, 4, 4), **f)
+    with _on_device(proj):
+        _native.call("fmhc_k2_fwd", proj.data_ptr(), params.data_ptr(), perm.data_ptr(),
+                     h_pre.data_ptr(), h_post.data_ptr(), H.data_ptr(), T, _stream(proj))
+    return h_pre, h_post, H
+
+
+@torch.library.impl(_lib, "mhc_coeffs_backward", "CUDA")
+def _mhc_coeffs_backward_cuda(grad_h_pre, grad_h_post, grad_H_merged, proj, alpha_pre,
+                              alpha_post, alpha_res, bias, perm):
+    proj, params, perm = _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm)
+    T = proj.shape[0]
+    g1, g2, g3 = _coef(grad_h_pre), _coef(grad_h_post), _coef(grad_H_merged)
+    grad_proj = torch.empty_like(proj)
+    grad_params = torch.empty((35,), device=proj.device, dtype=torch.float32)
+    with _on_device(proj):
+        ws_bytes = int(_native.lib().fmhc_k2_bwd_workspace_size(T))
+        ws = torch.empty(max(ws_bytes, 1), device=proj.device, dtype=torch.uint8)
+        _native.call("fmhc_k2_bwd", proj.data_ptr(), params.data_ptr(), perm.data_ptr(),
+                     g1.data_ptr(), g2.data_ptr(), g3.data_ptr(), grad_proj.data_ptr(),
+                     grad_params.data_ptr(), ws.data_ptr(), ws_bytes, T, _stream(proj))
+    return grad_proj, grad_params
+
+
 @torch.library.impl(_lib, "fused_pre_map", "CUDA")
 def _fused_pre_map_cuda(x_streams: torch.Tensor, h_pre: torch.Tensor):
     T, n, C = x_streams.shape
@@ -254,6 +329,36 @@ def _fused_pre_map_backward_cuda(grad_out, x_streams, h_pre):
         _native.call("fmhc_k3_bwd", grad_out.data_ptr(), x_streams.data_ptr(), h_pre.data_ptr(),
                      grad_x.data_ptr(), grad_h_pre.data_ptr(), T, n, C, _stream(x_streams))
     return grad_x, grad_h_pre
+
+
+@torch.library.impl(_lib, "pre_map_grad_h", "CUDA")
+def _pre_map_grad_h_cuda(grad_out, x_streams, h_pre):
+    T, n, C = x_streams.shape
+    _n4("pre_map_grad_h", n)
+    grad_out = _bf16("grad_out", grad_out)
+    x_streams = _bf16("x_streams", x_streams)
+    h_pre = _coef(h_pre)
+    grad_h_pre = torch.empty((T, n), device=x_streams.device, dtype=torch.float32)
+    with _on_device(x_streams):
+        _native.call("fmhc_k3_bwd", grad_out.data_ptr(), x_streams.data_ptr(), h_pre.data_ptr(),
+                     None, grad_h_pre.data_ptr(), T, n, C, _stream(x_streams))
+    return grad_h_pre
+
+
+@torch.library.impl(_lib, "mhc_grad_x_combine", "CUDA")
+def _mhc_grad_x_combine_cuda(gx1, grad_layer_input, h_pre, gx4):
+    T, n, C = gx1.shape
+    _n4("mhc_grad_x_combine", n)
+    gx1 = _bf16("gx1", gx1)
+    gli = _bf16("grad_layer_input", grad_layer_input)
+    h_pre = _coef(h_pre)
+    gx4 = None if gx4 is None else _bf16("gx4", gx4)
+    grad_x = torch.empty_like(gx1)
+    with _on_device(gx1):
+        _native.call("fmhc_mhc_grad_x_combine", gx1.data_ptr(), gli.data_ptr(), h_pre.data_ptr(),
+                     None if gx4 is None else gx4.data_ptr(), grad_x.data_ptr(), T, n, C,
+                     _stream(gx1))
+    return grad_x
 
 
 @torch.library.impl(_lib, "fused_post_res", "CUDA")
@@ -328,6 +433,27 @@ def _fused_post_res_backward(ctx, grad_out):
     return torch.ops.flash_mhc.fused_post_res_backward(
         grad_out, x_streams, layer_output, H_merged, h_post)
 
+
+def _mhc_coeffs_setup(ctx, inputs, output):
+    proj, a_pre, a_post, a_res, bias, perm = inputs
+    ctx.save_for_backward(proj, a_pre, a_post, a_res, bias, perm)
+
+
+def _mhc_coeffs_backward(ctx, g_hpre, g_hpost, g_H):
+    proj, a_pre, a_post, a_res, bias, perm = ctx.saved_tensors
+    T = proj.shape[0]
+    z = lambda *s: torch.zeros(*s, device=proj.device, dtype=torch.float32)  # noqa: E731
+    g_hpre = z(T, 4) if g_hpre is None else g_hpre
+    g_hpost = z(T, 4) if g_hpost is None else g_hpost
+    g_H = z(T, 4, 4) if g_H is None else g_H
+    g_proj, gp = torch.ops.flash_mhc.mhc_coeffs_backward(
+        g_hpre, g_hpost, g_H, proj, a_pre, a_post, a_res, bias, perm)
+    return (g_proj, gp[0:1].view_as(a_pre).to(a_pre.dtype), gp[1:2].view_as(a_post).to(a_post.dtype),
+            gp[2:3].view_as(a_res).to(a_res.dtype), gp[3:35].view_as(bias).to(bias.dtype), None)
+
+
+torch.library.register_autograd(
+    "flash_mhc::mhc_coeffs", _mhc_coeffs_backward, setup_context=_mhc_coeffs_setup)
 
 torch.library.register_autograd(
     "flash_mhc::fused_rmsnorm_project",

@@ -145,7 +145,8 @@ FMHC_API int fmhc_k3_fwd(const void *x, const float *h_pre, void *out,
  *   grad_x[t,j,c] = bf16( h_pre[t,j] * go[t,c] )
  *   grad_h[t,j]   = sum_c x[t,j,c] * go[t,c]                         (f32)
  * grad_out (T, C) bf16, x (T, n, C) bf16, h_pre (T, n) f32
- * -> grad_x (T, n, C) bf16, grad_h (T, n) f32.
+ * -> grad_x (T, n, C) bf16, grad_h (T, n) f32.  grad_x may be NULL: then only
+ * grad_h is computed (grad_x is then formed by fmhc_mhc_grad_x_combine).
  * Replaces op flash_mhc::fused_pre_map_backward (src/flash_mhc/ops.py:32-34,
  * 417-493) and kernel _fused_pre_map_bwd_fused_kernel_n4
  * (src/flash_mhc/kernels.py:720-853).
@@ -180,6 +181,49 @@ FMHC_API int fmhc_k4_bwd(const void *grad_out, const void *x, const void *lo,
                 const float *H, const float *h_post,
                 void *grad_x, void *grad_lo, float *grad_H, float *grad_hp,
                 int64_t T, int64_t n, int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * Gradient of the residual streams from the three paths that read them:
+ *   grad_x[t,j,c] = bf16( gx1[t,j,c] + h_pre[t,j] * grad_li[t,c] + gx4[t,j,c] )
+ * gx1: K1's grad_x (T, n, C) bf16; grad_li: the gradient of the layer input
+ * (T, C) bf16 (K3's upstream gradient); gx4: K4's grad_x (T, n, C) bf16 or
+ * NULL; h_pre (T, n) f32.  grad_x may alias gx1.  One pass instead of K3's
+ * grad_x write plus two separate additions.
+ * No counterpart in the reference (its autograd engine sums three tensors).
+ */
+FMHC_API int fmhc_mhc_grad_x_combine(const void *gx1, const void *grad_li, const float *h_pre,
+                                     const void *gx4, void *grad_x, int64_t T, int64_t n,
+                                     int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * K2 forward: the per-token coefficient math on the 32 projection logits
+ * (n = 4, D = 32), one launch.
+ *   h_pre  = sigmoid(a_pre  * proj[:, 0:4]  + bias[0:4])
+ *   h_post = 2 sigmoid(a_post * proj[:, 4:8] + bias[4:8])
+ *   a      = softmax(a_res * proj[:, 8:32] + bias[8:32])
+ *   H_merged[i][j] = sum_k a[k] perm[k][4i+j] - h_post[i] h_pre[j]
+ * proj (T, 32) bf16; params (35,) f32 = [a_pre, a_post, a_res, bias[32]];
+ * perm (24, 16) f32 -> h_pre, h_post (T, 4) f32, H_merged (T, 4, 4) f32, each
+ * rounded to bf16 like the reference (which computes K2 in the input dtype).
+ * Replaces the eager K2 of the caller (src/flash_mhc/block.py:150-170),
+ * ~20 torch launches.
+ */
+FMHC_API int fmhc_k2_fwd(const void *proj, const float *params, const float *perm,
+                         float *h_pre, float *h_post, float *H_merged, int64_t T,
+                         void *stream);
+
+/* ------------------------------------------------------------------------
+ * K2 backward: given the f32 gradients of h_pre, h_post and H_merged, returns
+ * grad_proj (T, 32) bf16 and grad_params (35,) f32 (summed over tokens in a
+ * fixed order, deterministic).  `workspace` (256-byte aligned) holds per-block
+ * partial sums; size from fmhc_k2_bwd_workspace_size(T).
+ * Replaces the torch autograd backward of the eager K2 (src/flash_mhc/block.py:150-170).
+ */
+FMHC_API int64_t fmhc_k2_bwd_workspace_size(int64_t T);
+FMHC_API int fmhc_k2_bwd(const void *proj, const float *params, const float *perm,
+                         const float *grad_h_pre, const float *grad_h_post,
+                         const float *grad_H_merged, void *grad_proj, float *grad_params,
+                         void *workspace, int64_t workspace_bytes, int64_t T, void *stream);
 
 #ifdef __cplusplus
 }

@@ -85,7 +85,15 @@ def test_block_matches_float64_oracle():
                   bias=blk.W_all.bias.detach().float().cpu().numpy(), perm=g["perm"],
                   Wl=blk.layer.proj.weight.detach().float().cpu().numpy())
     r = O.block_forward_backward(params, g["x"], g["g"], rms_eps=1e-6)
-    assert_close("out", out.detach().float().cpu().numpy(), r["out"], 2e-2, 1e-2)
+    # h_pre, h_post and H_merged are rounded to bf16 (as in the reference), an
+    # error of up to 2^-8 of their magnitude that the output multiplies by |x|
+    # and |layer_output|: bound = 2e-2 + 1e-2|ref| + 2^-8 (sum_j |x_j| + |lo|).
+    got = out.detach().float().cpu().numpy()
+    cond = np.abs(g["x"]).sum(axis=1, keepdims=True) + np.abs(
+        O.gelu(r["layer_input"] @ params["Wl"].T))[:, None, :]
+    lim = 2e-2 + 1e-2 * np.abs(r["out"]) + 2.0 ** -8 * cond
+    diff = np.abs(got - r["out"])
+    assert np.all(diff <= lim), f"out vs oracle: worst {np.max(diff / lim):.3g} x bound"
     assert_close("grad_x", x.grad.float().cpu().numpy(), r["grad_x"], 1e-1, 5e-2)
 
 
@@ -148,7 +156,16 @@ def test_eval_no_grad_tiny_T_with_outliers(T):
         out = blk(xb)
         ref = blk._forward_pytorch(xb)
     assert out.shape == (T, 4, C)
-    torch.testing.assert_close(out.float(), ref.float(), atol=5e-2, rtol=2e-2)
+    # Both paths round the coefficients to bf16 but at different points (the
+    # fused K2 keeps f32 intermediates), so they may differ by one bf16 step of
+    # a coefficient, multiplied by |x| (x100 in the outlier channels) and by
+    # |layer_output|: bound = 5e-2 + 2e-2|ref| + 2^-7 (sum_j |x_j| + |lo|).
+    with torch.no_grad():
+        lo = blk.layer(blk._mhc_pre_map_pytorch(xb)[0]).float()
+    cond = xb.float().abs().sum(dim=1, keepdim=True) + lo.abs()[:, None, :]
+    lim = 5e-2 + 2e-2 * ref.float().abs() + 2.0 ** -7 * cond
+    diff = (ref.float() - out.float()).abs()
+    assert bool((diff <= lim).all()), float((diff / lim).max())
     params = dict(alpha_pre=0.01, alpha_post=0.01, alpha_res=0.01,
                   W=blk.W_all.weight.detach().float().cpu().numpy(),
                   bias=blk.W_all.bias.detach().float().cpu().numpy(),

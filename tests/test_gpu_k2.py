@@ -1,0 +1,105 @@
+"""GPU parity of the fused K2 kernels (flash_mhc::mhc_coeffs and its backward).
+
+* forward against the reference's eager K2 in bf16 (the block's own
+  `_coeffs_from_proj`, i.e. src/flash_mhc/block.py:161-169, on the same GPU):
+  the outputs are rounded to bf16 in both, so they agree to one bf16 step;
+* forward and backward against the float64 oracle (oracle.mhc_oracle.k2_coeffs
+  and its hand-derived backward): bf16 outputs within 1e-2 + 1e-2*|ref|
+  (bf16 rounding of the coefficients), parameter gradients (sums over T)
+  within 2e-2 * sum|terms| scale.
+"""
+
+from __future__ import annotations
+
+import numpy as np
+import pytest
+import torch
+
+import flash_mhc  # noqa: F401
+from flash_mhc import MHCLiteBlock
+from oracle import mhc_oracle as O
+from tests._util import assert_close
+
+pytestmark = [
+    pytest.mark.gpu,
+    pytest.mark.skipif(not torch.cuda.is_available(), reason="needs a CUDA device"),
+]
+
+
+def _setup(T, seed, alphas=(0.7, 0.9, 1.3), scale=1.0):
+    torch.manual_seed(seed)
+    blk = MHCLiteBlock(4, 16, torch.nn.Identity()).cuda()
+    with torch.no_grad():
+        blk.alpha_pre.fill_(alphas[0]); blk.alpha_post.fill_(alphas[1]); blk.alpha_res.fill_(alphas[2])
+        blk.W_all.bias.normal_(0.0, 0.5)
+    proj = (torch.randn(T, 32, device="cuda") * scale).bfloat16()
+    return blk, proj
+
+
+@pytest.mark.parametrize("T,scale", [(1, 1.0), (257, 1.0), (4096, 3.0), (65536, 1.0)])
+def test_k2_forward_matches_reference_eager_bf16(T, scale):
+    blk, proj = _setup(T, 1, scale=scale)
+    h_pre, h_post, H = torch.ops.flash_mhc.mhc_coeffs(proj, blk.alpha_pre, blk.alpha_post,
+                                                      blk.alpha_res, blk.W_all.bias, blk.perm_mat)
+    with torch.no_grad():
+        r_pre, r_post, r_H = blk._coeffs_from_proj(proj, torch.bfloat16)
+    torch.testing.assert_close(h_pre, r_pre.float(), atol=1e-2, rtol=1e-2)
+    torch.testing.assert_close(h_post, r_post.float(), atol=2e-2, rtol=1e-2)
+    torch.testing.assert_close(H, r_H.float(), atol=2e-2, rtol=2e-2)
+    # outputs are bf16-representable, like the reference's .float() of bf16 tensors
+    for t in (h_pre, h_post, H):
+        assert torch.equal(t, t.bfloat16().float())
+
+
+def _oracle_params(blk):
+    return dict(ap=float(blk.alpha_pre), aq=float(blk.alpha_post), ar=float(blk.alpha_res),
+                bias=O.bf16_round(blk.W_all.bias.detach().float().cpu().numpy()),
+                perm=blk.perm_mat.float().cpu().numpy())
+
+
+@pytest.mark.parametrize("T", [3, 1000])
+def test_k2_forward_backward_match_float64_oracle(T):
+    blk, proj = _setup(T, 2)
+    p = _oracle_params(blk)
+    ap, aq, ar = (float(O.bf16_round(np.float32(v))) for v in (p["ap"], p["aq"], p["ar"]))
+    pr = proj.float().cpu().numpy()
+    ctx = O.k2_coeffs(pr, ap, aq, ar, p["bias"], p["perm"])
+    with torch.no_grad():
+        a, b, c = torch.ops.flash_mhc.mhc_coeffs(proj, blk.alpha_pre, blk.alpha_post,
+                                                 blk.alpha_res, blk.W_all.bias, blk.perm_mat)
+    assert_close("h_pre", a.cpu().numpy(), ctx["h_pre"], 1e-2, 1e-2)
+    assert_close("h_post", b.cpu().numpy(), ctx["h_post"], 1e-2, 1e-2)
+    assert_close("H_merged", c.cpu().numpy(), ctx["H_merged"], 2e-2, 2e-2)
+
+    g = torch.Generator(device="cuda").manual_seed(5)
+    g_hpre = torch.randn(T, 4, device="cuda", generator=g)
+    g_hpost = torch.randn(T, 4, device="cuda", generator=g)
+    g_H = torch.randn(T, 4, 4, device="cuda", generator=g)
+    with torch.no_grad():
+        g_proj, gp = torch.ops.flash_mhc.mhc_coeffs_backward(
+            g_hpre, g_hpost, g_H, proj, blk.alpha_pre, blk.alpha_post, blk.alpha_res,
+            blk.W_all.bias, blk.perm_mat)
+    rg = O.k2_coeffs_bwd(ctx, g_hpre.cpu().numpy(), g_hpost.cpu().numpy(), g_H.cpu().numpy(),
+                         ap, aq, ar, p["perm"])
+    r_proj, r_ap, r_aq, r_ar, r_bias = rg
+    assert_close("grad_proj", g_proj.float().cpu().numpy(), r_proj, 2e-2, 2e-2)
+    ref_params = np.concatenate([[r_ap, r_aq, r_ar], r_bias])
+    got = gp.cpu().numpy()
+    scale = np.maximum(np.abs(ref_params), np.sqrt(T))  # sums over T of O(1) terms
+    assert np.all(np.abs(got - ref_params) <= 2e-2 * scale), (got, ref_params)
+
+
+def test_k2_autograd_through_block_params():
+    """d(loss)/d(params) of mhc_coeffs via autograd equals the backward op."""
+    blk, proj = _setup(512, 3)
+    proj = proj.requires_grad_(True)
+    a, b, c = torch.ops.flash_mhc.mhc_coeffs(proj, blk.alpha_pre, blk.alpha_post, blk.alpha_res,
+                                             blk.W_all.bias, blk.perm_mat)
+    loss = (a * 1.5).sum() + (b * -0.5).sum() + (c * 2.0).sum()
+    loss.backward()
+    g_proj, gp = torch.ops.flash_mhc.mhc_coeffs_backward(
+        torch.full_like(a, 1.5), torch.full_like(b, -0.5), torch.full_like(c, 2.0), proj.detach(),
+        blk.alpha_pre, blk.alpha_post, blk.alpha_res, blk.W_all.bias, blk.perm_mat)
+    assert torch.equal(proj.grad, g_proj)
+    assert torch.equal(blk.W_all.bias.grad, gp[3:])
+    assert torch.equal(blk.alpha_res.grad, gp[2:3])

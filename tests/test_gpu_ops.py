@@ -312,3 +312,23 @@ def test_k1_tensor_core_kernels_are_bitwise_deterministic_at_metric_shape():
     gos = (go.float() * inv0[:, None]).bfloat16().float()
     rgW = gos.t() @ xf.float()
     torch.testing.assert_close(gW0.float(), rgW, atol=BF_ATOL, rtol=BF_RTOL)
+
+
+@pytest.mark.parametrize("T,C", [(300, 768), (40, 100), (33, 97)])
+def test_block_backward_pieces(T, C):
+    """pre_map_grad_h (K3 backward without grad_x) and the one-pass grad_x
+    combination used by the fused block backward."""
+    d = _inputs(T, C, 60 + T)
+    x, hp, gli = _bf(d["x"]), _f32(d["hp"]), _bf(d["g_pre"])
+    gx_ref, gh_ref = torch.ops.flash_mhc.fused_pre_map_backward(gli, x, hp)
+    gh = torch.ops.flash_mhc.pre_map_grad_h(gli, x, hp)
+    assert torch.equal(gh, gh_ref)
+    g = torch.Generator(device="cuda").manual_seed(T)
+    gx1 = torch.randn(T, 4, C, device="cuda", generator=g).bfloat16()
+    gx4 = torch.randn(T, 4, C, device="cuda", generator=g).bfloat16()
+    for extra in (gx4, None):
+        out = torch.ops.flash_mhc.mhc_grad_x_combine(gx1, gli, hp, extra)
+        ref = gx1.float() + hp[:, :, None] * gli.float()[:, None, :]
+        if extra is not None:
+            ref = ref + extra.float()
+        torch.testing.assert_close(out.float(), ref, atol=BF_ATOL, rtol=BF_RTOL)
