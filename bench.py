@@ -296,6 +296,9 @@ def run_ours(args):
     # --- the whole block ------------------------------
     block = None if args.no_block else run_block(args, torch, dist, world, dev)
 
+    # --- small per-GPU batch: eager vs CUDA-graph replay -------------------
+    graphs = None if args.no_graphs else run_small_graphs(args, torch, dev)
+
     if rank == 0:
         peaks = measured_peaks()
         bm = bytes_model(T, C)
@@ -329,6 +332,7 @@ def run_ours(args):
             "kernels": kernels,
             "e2e": e2e,
             "block": block,
+            "small_batch_graphs": graphs,
             "gpu_launches": HotPath.LAUNCHES_PER_STEP * args.steps,
             "clocks": clk.summary(),
             "native_lib": os.path.relpath(lib_path, ROOT),
@@ -350,6 +354,45 @@ def _physical_gpu_indices(world):
         except ValueError:
             pass
     return list(range(world))
+
+
+def run_small_graphs(args, torch, dev):
+    """The hot-path step at a small per-GPU batch (the 8-GPU strong-scaling
+    shard of the metric batch, T = 65536/8), launched eagerly and replayed
+    from a CUDA graph; host launch overhead dominates the eager step here."""
+    T = args.small_T
+    hp = HotPath(T, args.C, dev, seed=99, torch=torch)
+    n = 50
+
+    def timed(fn):
+        for _ in range(5):
+            fn()
+        torch.cuda.synchronize()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        for _ in range(n):
+            fn()
+        e.record()
+        torch.cuda.synchronize()
+        return s.elapsed_time(e) / n
+
+    eager_ms = timed(lambda: hp.step(hp.inputs))
+    side = torch.cuda.Stream()
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        for _ in range(2):
+            hp.step(hp.inputs)
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        hp.step(hp.inputs)
+    graph_ms = timed(graph.replay)
+    del graph
+    return {"T_per_gpu": T, "C": args.C, "steps": n,
+            "eager_ms_per_step": round(eager_ms, 4), "graph_ms_per_step": round(graph_ms, 4),
+            "eager_tokens_per_s": round(T / (eager_ms * 1e-3), 1),
+            "graph_tokens_per_s": round(T / (graph_ms * 1e-3), 1)}
 
 
 def run_block(args, torch, dist, world, dev):
@@ -592,6 +635,8 @@ def main():
     ap.add_argument("--no-block", action="store_true", help="skip the MHCLiteBlock measurement")
     ap.add_argument("--block-T", type=int, default=65536, help="tokens per GPU for the block")
     ap.add_argument("--block-C", type=int, default=2048)
+    ap.add_argument("--no-graphs", action="store_true", help="skip the small-batch graph measurement")
+    ap.add_argument("--small-T", type=int, default=8192)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: the timing rules ask for >= 3 warm-up steps", file=sys.stderr)

@@ -14,6 +14,8 @@
 #include "fmhc_common.cuh"
 #include "fmhc_launch.h"
 
+#include <mutex>
+
 namespace fmhc {
 
 using bf16 = __nv_bfloat16;
@@ -188,10 +190,14 @@ int64_t k1_dw_workspace_bytes(int64_t T, int64_t nC, int64_t D) {
 
 namespace {
 int sm_count() {
-  int dev = 0, sms = 0;
+  static std::mutex mu;
+  static int cache[16] = {};
+  int dev = 0;
   cudaGetDevice(&dev);
-  cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-  return sms;
+  if (dev < 0 || dev >= 16) dev = 15;
+  std::lock_guard<std::mutex> lock(mu);
+  if (!cache[dev]) cudaDeviceGetAttribute(&cache[dev], cudaDevAttrMultiProcessorCount, dev);
+  return cache[dev];
 }
 int warp_grid(int64_t T) {
   const int64_t cap = int64_t(sm_count()) * 8;  // 8 blocks of 8 warps per SM

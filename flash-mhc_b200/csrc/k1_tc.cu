@@ -25,6 +25,7 @@
 #include <cudaTypedefs.h>
 
 #include <cstdio>
+#include <mutex>
 
 #include "fmhc_common.cuh"
 #include "k1_tc.h"
@@ -310,12 +311,17 @@ int device_sms() {
   return sms;
 }
 
-// Opt in to the kernel's dynamic shared memory once per (kernel, device).
+// Opt in to the kernel's dynamic shared memory once per (kernel, device) for
+// the whole process (not per thread: autograd runs backward ops on its own
+// threads, and a first-time attribute call must not land inside a CUDA-graph
+// capture made on another thread).
 int set_smem_attr(const void *kernel, size_t bytes) {
-  static thread_local const void *done_kernel[8][16] = {};
+  static std::mutex mu;
+  static const void *done_kernel[8][16] = {};
   int dev = 0;
   cudaGetDevice(&dev);
   if (dev < 0 || dev >= 16) dev = 15;
+  std::lock_guard<std::mutex> lock(mu);
   for (int i = 0; i < 8; ++i) {
     if (done_kernel[i][dev] == kernel) return 0;
     if (done_kernel[i][dev] == nullptr) {

@@ -16,6 +16,8 @@
 #include "fmhc_common.cuh"
 #include "fmhc_launch.h"
 
+#include <mutex>
+
 // Chunks per lane in flight (U) and minimum resident blocks per SM (MINB,
 // bounds registers) of each kernel; chosen by measurement at T=65536, C=1024.
 #ifndef FMHC_K3F_U
@@ -354,28 +356,42 @@ grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli
 }
 
 // ------------------------------------------------------------------ launchers
-namespace {
-
+// Resident blocks per SM of `kernel` and the SM count, cached for the process
+// (occupancy queries and attribute reads stay out of CUDA-graph captures and
+// out of the per-launch cost).
 template <class K>
 int grid_for(K kernel, int64_t T, int threads) {
-  // Persistent-style grid: as many resident blocks as the SMs hold, never more
-  // warps than tokens.
-  static thread_local int cached_dev = -1, sms = 0;
+  struct Entry {
+    const void *k;
+    int dev, per_sm, sms;
+  };
+  static std::mutex mu;
+  static Entry cache[64];
+  static int used = 0;
   int dev = 0;
   cudaGetDevice(&dev);
-  if (dev != cached_dev) {
-    cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
-    cached_dev = dev;
+  int per_sm = 0, sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(mu);
+    for (int i = 0; i < used; ++i)
+      if (cache[i].k == reinterpret_cast<const void *>(kernel) && cache[i].dev == dev) {
+        per_sm = cache[i].per_sm;
+        sms = cache[i].sms;
+      }
+    if (sms == 0) {
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, dev);
+      cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
+      if (per_sm < 1) per_sm = 1;
+      if (used < 64) cache[used++] = Entry{reinterpret_cast<const void *>(kernel), dev, per_sm, sms};
+    }
   }
-  int per_sm = 0;
-  cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, kernel, threads, 0);
-  if (per_sm < 1) per_sm = 1;
   const int64_t warps_per_block = threads / 32;
   const int64_t need = (T + warps_per_block - 1) / warps_per_block;
   const int64_t cap = int64_t(sms) * per_sm;
   return int(need < cap ? need : cap);
 }
 
+namespace {
 constexpr int kThreads = 256;
 
 }  // namespace
