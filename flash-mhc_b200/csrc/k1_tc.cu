@@ -9,14 +9,18 @@
 // in TMEM while the sum of squares is taken by CUDA cores from the same
 // shared-memory tiles.
 //
-// Persistent kernel, one CTA per SM, 6 warps:
+// Persistent kernel, FMHC_K1F_CTAS_PER_SM resident CTAs per SM, 6 warps:
 //   warp 0     TMA producer: x tile (<=128 rows x 64 k, four 32-row boxes,
 //              128-byte swizzle) + W chunk (32 x 64) per pipeline stage;
 //   warp 1     MMA issuer: 4 x tcgen05.mma M128 N32 K16 per stage into one of
 //              two TMEM accumulators (64 columns allocated);
 //   warps 2-5  one thread per tile row: sum of squares from shared memory,
 //              then the epilogue (tcgen05.ld of the row's 32 f32 columns,
-//              scale by inv_rms, bf16 store).
+//              scale by inv_rms, bf16 store).  These threads read the stage
+//              with ordinary (generic-proxy) loads while its refill is a TMA
+//              (async-proxy) write, so each thread issues fence.proxy.async
+//              before its release arrive; without it, loads still pending at
+//              the arrive were seen returning the next fill's data.
 // Each CTA owns a contiguous token range in 32-row units (balanced to within
 // 32 rows across CTAs); partial tiles load only the 32-row boxes they need.
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on expiry the kernel records
@@ -39,11 +43,18 @@ using namespace sm100;
 // A stage holds kColBoxes column boxes of 64 k (one 128-byte swizzled row
 // each) for up to 128 rows, so every x row is read kColBoxes * 128 contiguous
 // bytes at a time.
+// Defaults measured at T=65536, nC=4096: two resident CTAs per SM, each with
+// four 20 KiB stages, reach ~92% of the HBM copy bandwidth (one CTA with five
+// 40 KiB stages: ~84%).
 #ifndef FMHC_K1F_COLBOXES
-#define FMHC_K1F_COLBOXES 2
+#define FMHC_K1F_COLBOXES 1
 #endif
 #ifndef FMHC_K1F_STAGES
-#define FMHC_K1F_STAGES (FMHC_K1F_COLBOXES == 1 ? 8 : 5)
+#define FMHC_K1F_STAGES 4
+#endif
+// Resident CTAs per SM (each with its own pipeline and token range).
+#ifndef FMHC_K1F_CTAS_PER_SM
+#define FMHC_K1F_CTAS_PER_SM 2
 #endif
 constexpr int kBM = 128;            // tile rows (MMA M)
 constexpr int kColBoxes = FMHC_K1F_COLBOXES;
@@ -58,6 +69,7 @@ constexpr int kBBytes = kColBoxes * kColBBytes;
 constexpr int kBoxBytes = kBoxRows * 64 * 2;   // 4 KiB: 32 rows of one column box
 constexpr int kStageBytes = kABytes + kBBytes;
 constexpr int kThreads = 192;
+constexpr int kRowThreads = 128;    // warps 2-5: sumsq + epilogue
 constexpr uint32_t kTmemCols = 64;  // two 32-column accumulators
 constexpr float kEps = 1e-6f;
 
@@ -76,7 +88,7 @@ struct alignas(1024) FwdSmem {
 enum : unsigned { kSiteProdEmpty = 0x101, kSiteMmaFull = 0x102, kSiteMmaTempty = 0x103,
                   kSiteEpiFull = 0x104, kSiteEpiTfull = 0x105, kSiteDrain = 0x106 };
 
-__global__ void __launch_bounds__(kThreads, 1)
+__global__ void __launch_bounds__(kThreads, FMHC_K1F_CTAS_PER_SM)
 k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_w, __nv_bfloat16 *__restrict__ out,
                  float *__restrict__ inv_rms, int64_t T, int nC, int64_t units) {
@@ -98,7 +110,9 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   if (threadIdx.x == 0) {
     for (int s = 0; s < kStages; ++s) {
       mbar_init(smem_u32(&sm.full[s]), 1);
-      mbar_init(smem_u32(&sm.empty[s]), 1 + 4);  // MMA commit + 4 row warps
+      // MMA commit + every row-warp thread: each thread fences and releases
+      // its own shared-memory reads before the TMA may refill the stage.
+      mbar_init(smem_u32(&sm.empty[s]), 1 + kRowThreads);
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(smem_u32(&sm.tfull[b]), 1);
@@ -200,27 +214,32 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     for (int tile = 0; tile < ntiles && !*abort; ++tile) {
       const int64_t row0 = t_begin + int64_t(tile) * kBM;
       const int64_t rows = (t_end - row0) < kBM ? (t_end - row0) : kBM;
-      float ss = 0.f;
+      // Eight independent partial sums (one per bf16 lane of a 16-byte chunk)
+      // keep the FMA pipe busy instead of one serial chain per thread.
+      float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       bool ok = true;
       for (int kb = 0; kb < nk; ++kb) {
         if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteEpiFull)) { ok = false; break; }
 #pragma unroll
         for (int cb = 0; cb < kColBoxes; ++cb) {
-        const uint8_t *row = sm.stage[stage] + cb * kColABytes + r * 128;
+          const uint8_t *row = sm.stage[stage] + cb * kColABytes + r * 128;
+          uint4 u[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) {
-          // Any order covers the row; rotating by r keeps the 8 rows of a
-          // swizzle atom on distinct banks.
-          const uint4 u = *reinterpret_cast<const uint4 *>(row + (((i + r) & 7) << 4));
-          float f;
-          f = bf16lo(u.x); ss = fmaf(f, f, ss); f = bf16hi(u.x); ss = fmaf(f, f, ss);
-          f = bf16lo(u.y); ss = fmaf(f, f, ss); f = bf16hi(u.y); ss = fmaf(f, f, ss);
-          f = bf16lo(u.z); ss = fmaf(f, f, ss); f = bf16hi(u.z); ss = fmaf(f, f, ss);
-          f = bf16lo(u.w); ss = fmaf(f, f, ss); f = bf16hi(u.w); ss = fmaf(f, f, ss);
+          for (int i = 0; i < 8; ++i)  // rotate by r: the 8 rows of a swizzle atom hit distinct banks
+            u[i] = *reinterpret_cast<const uint4 *>(row + (((i + r) & 7) << 4));
+#pragma unroll
+          for (int i = 0; i < 8; ++i) {
+            float f;
+            f = bf16lo(u[i].x); ss8[0] = fmaf(f, f, ss8[0]); f = bf16hi(u[i].x); ss8[1] = fmaf(f, f, ss8[1]);
+            f = bf16lo(u[i].y); ss8[2] = fmaf(f, f, ss8[2]); f = bf16hi(u[i].y); ss8[3] = fmaf(f, f, ss8[3]);
+            f = bf16lo(u[i].z); ss8[4] = fmaf(f, f, ss8[4]); f = bf16hi(u[i].z); ss8[5] = fmaf(f, f, ss8[5]);
+            f = bf16lo(u[i].w); ss8[6] = fmaf(f, f, ss8[6]); f = bf16hi(u[i].w); ss8[7] = fmaf(f, f, ss8[7]);
+          }
         }
-        }
-        __syncwarp();
-        if (lane == 0) mbar_arrive(smem_u32(&sm.empty[stage]));
+        // The refill is a TMA (async-proxy) write: order this thread's
+        // generic-proxy reads of the stage before it, then release.
+        fence_proxy_async_smem();
+        mbar_arrive(smem_u32(&sm.empty[stage]));
         if (++stage == kStages) { stage = 0; phase ^= 1; }
       }
       if (!ok) break;
@@ -235,6 +254,7 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       if (++acc == 2) { acc = 0; acc_phase ^= 1; }
       if (r < rows) {
         const int64_t t = row0 + r;
+        const float ss = ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
         const float inv = rsqrtf(ss / float(nC) + kEps);
         uint4 *o = reinterpret_cast<uint4 *>(out + t * kND);
 #pragma unroll
@@ -351,8 +371,10 @@ bool device_is_sm100() {
 
 const char *k1_tc_error() { return k1tc::g_msg; }
 
-static_assert(sizeof(k1tc::BwdSmem) + 1024 <= 232448, "K1 backward shared memory");
-static_assert(sizeof(k1tc::FwdSmem) + 1024 <= 232448, "K1 forward shared memory");
+static_assert((sizeof(k1tc::BwdSmem) + 1024) * FMHC_K1B_CTAS_PER_SM <= 232448,
+              "K1 backward shared memory");
+static_assert((sizeof(k1tc::FwdSmem) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
+              "K1 forward shared memory");
 
 bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
                          int64_t T, int64_t nC, int64_t D) {
@@ -375,7 +397,7 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
     return 5;
   }
   const int64_t units = (T + kBoxRows - 1) / kBoxRows;
-  int64_t grid = device_sms();
+  int64_t grid = int64_t(device_sms()) * FMHC_K1F_CTAS_PER_SM;
   if (grid > units) grid = units;
   const size_t smem = sizeof(FwdSmem) + 1024;
   if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_kernel), smem)) return e;
@@ -401,8 +423,9 @@ BwdPlan bwd_plan(int64_t T, int64_t nC) {
   p.ntt = int((T + kBwdBT - 1) / kBwdBT);
   p.nkc = int(nC / kBwdBK);
   p.units = int64_t(p.nkc) * p.ntt;
-  int64_t g = device_sms();
+  int64_t g = int64_t(device_sms()) * FMHC_K1B_CTAS_PER_SM;
   if (g > p.units) g = p.units;
+  if (g > kRedMaxContrib) g = kRedMaxContrib;  // every contributor must fit the reduce table
   if (g < 1) g = 1;
   p.grid = int(g);
   p.maxseg = 1;
@@ -493,8 +516,7 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.with_dw = with_dw ? 1 : 0;
   k1_bwd_tc_kernel<<<unsigned(p.grid), kBwdThreads, smem, s>>>(mx, mgx, mgo, mgos, mw, args);
   if (with_dw) {
-    const int64_t n = int64_t(kND) * nC;
-    k1_bwd_dw_reduce_kernel<<<unsigned((n + 255) / 256), 256, 0, s>>>(
+    k1_bwd_dw_reduce_kernel<<<dim3(unsigned(p.nkc), kND / 8), 256, 0, s>>>(
         part, static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.units, p.grid, p.maxseg);
   }
   return 0;

@@ -35,9 +35,24 @@
 namespace fmhc {
 namespace k1tc {
 
+#ifndef FMHC_K1B_STAGES
+#define FMHC_K1B_STAGES 4
+#endif
+#ifndef FMHC_K1B_CTAS_PER_SM
+#define FMHC_K1B_CTAS_PER_SM 1
+#endif
+#ifndef FMHC_K1B_ACC_BUFS   // grad_x TMEM accumulators (1 or 2)
+#define FMHC_K1B_ACC_BUFS 2
+#endif
+#ifndef FMHC_K1B_W_BUFS     // W chunk buffers (1 or 2)
+#define FMHC_K1B_W_BUFS 2
+#endif
 constexpr int kBwdBT = 128;                       // tokens per unit (MMA M of grad_x)
 constexpr int kBwdBK = 128;                       // k per unit (MMA N of grad_x, M of grad_W)
-constexpr int kBwdStages = 4;
+constexpr int kBwdStages = FMHC_K1B_STAGES;
+constexpr int kBwdAcc = FMHC_K1B_ACC_BUFS;
+constexpr int kBwdWBufs = FMHC_K1B_W_BUFS;
+static_assert(kBwdAcc == 1 || kBwdAcc == 2, "one or two grad_x accumulators");
 constexpr int kBwdXBytes = kBwdBT * kBwdBK * 2;   // 32 KiB (two 16 KiB boxes)
 constexpr int kBwdXBox = kBwdBT * 64 * 2;         // 16 KiB
 constexpr int kBwdGBytes = kBwdBT * kND * 2;      // 8 KiB  (go or gos tile)
@@ -45,19 +60,21 @@ constexpr int kBwdSBytes = kBwdBT * 8;            // 1 KiB  ((s, inv_rms) per to
 constexpr int kBwdStageBytes = kBwdXBytes + 2 * kBwdGBytes + kBwdSBytes;  // 49 KiB
 constexpr int kBwdThreads = 320;                  // producer, MMA, 8 epilogue warps
 constexpr int kBwdEpiWarps = 8;
+constexpr int kRedMaxContrib = 1024;              // >= grid (bwd_plan clamps the grid to it)
 constexpr int kBwdWBytes = kND * kBwdBK * 2;      // 8 KiB  (two 4 KiB boxes)
-constexpr uint32_t kBwdTmemCols = 512;            // 2 x 128 (grad_x) + 32 (grad_W)
-constexpr uint32_t kBwdDwCol = 256;
+// kBwdAcc x 128 (grad_x) + 32 (grad_W) columns, rounded up to a power of two.
+constexpr uint32_t kBwdTmemCols = kBwdAcc == 2 ? 512 : 256;
+constexpr uint32_t kBwdDwCol = kBwdAcc * 128;
 
 struct alignas(1024) BwdSmem {
   uint8_t stage[kBwdStages][kBwdStageBytes];
-  uint8_t wbuf[2][kBwdWBytes];
+  uint8_t wbuf[kBwdWBufs][kBwdWBytes];
   uint64_t full[kBwdStages];
   uint64_t empty[kBwdStages];
-  uint64_t tfull[2];
-  uint64_t tempty[2];
-  uint64_t wfull[2];
-  uint64_t wempty[2];
+  uint64_t tfull[kBwdAcc];
+  uint64_t tempty[kBwdAcc];
+  uint64_t wfull[kBwdWBufs];
+  uint64_t wempty[kBwdWBufs];
   uint64_t dwfull;
   uint64_t dwempty;
   // epi[i & 1]: the 4 epilogue warps finished writing grad_x of local unit i.
@@ -96,7 +113,7 @@ __device__ __forceinline__ void bwd_unit(int64_t u, int ntt, int &kc, int &tt) {
   tt = int(u - int64_t(kc) * ntt);
 }
 
-__global__ void __launch_bounds__(kBwdThreads, 1)
+__global__ void __launch_bounds__(kBwdThreads, FMHC_K1B_CTAS_PER_SM)
 k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_gx,
                  const __grid_constant__ CUtensorMap tmap_go,
@@ -117,9 +134,11 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       mbar_init(smem_u32(&sm.full[s]), 1);
       mbar_init(smem_u32(&sm.empty[s]), 1);  // released by the epilogue after its store read
     }
-    for (int b = 0; b < 2; ++b) {
+    for (int b = 0; b < kBwdAcc; ++b) {
       mbar_init(smem_u32(&sm.tfull[b]), 1);
       mbar_init(smem_u32(&sm.tempty[b]), kBwdEpiWarps);
+    }
+    for (int b = 0; b < kBwdWBufs; ++b) {
       mbar_init(smem_u32(&sm.wfull[b]), 1);
       mbar_init(smem_u32(&sm.wempty[b]), 1);
     }
@@ -155,11 +174,12 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       for (int64_t u = u0; u < u1 && !*abort; ++u) {
         int kc, tt;
         bwd_unit(u, a.ntt, kc, tt);
-        if (kc != kc_prev) {  // new segment: W chunk into wbuf[seg & 1]
+        if (kc != kc_prev) {  // new segment: W chunk into wbuf[seg % kBwdWBufs]
           ++seg;
           kc_prev = kc;
-          const int wb = seg & 1;
-          if (!mbar_wait(smem_u32(&sm.wempty[wb]), ((seg >> 1) & 1) ^ 1, abort, kSiteBProdW)) break;
+          const int wb = seg % kBwdWBufs;
+          if (!mbar_wait(smem_u32(&sm.wempty[wb]), ((seg / kBwdWBufs) & 1) ^ 1, abort, kSiteBProdW))
+            break;
           const uint32_t wf = smem_u32(&sm.wfull[wb]);
           mbar_arrive_expect_tx(wf, kBwdWBytes);
           tma_load_2d(smem_u32(sm.wbuf[wb]), &tmap_w, wf, kc * kBwdBK, 0);
@@ -204,7 +224,9 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           if (a.with_dw && seg > 0 &&
               !mbar_wait(smem_u32(&sm.dwempty), (seg - 1) & 1, abort, kSiteBMmaDw))
             break;
-          if (!mbar_wait(smem_u32(&sm.wfull[seg & 1]), (seg >> 1) & 1, abort, kSiteBMmaW)) break;
+          if (!mbar_wait(smem_u32(&sm.wfull[seg % kBwdWBufs]), (seg / kBwdWBufs) & 1, abort,
+                         kSiteBMmaW))
+            break;
         }
         int kc_next = -1, tt_next;
         if (u + 1 < u1) bwd_unit(u + 1, a.ntt, kc_next, tt_next);
@@ -224,7 +246,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         }
         {
           // grad_x: M = tokens, N = 128 k (two 64-wide MN blocks 4 KiB apart), K = d.
-          const uint32_t wb = smem_u32(sm.wbuf[seg & 1]);
+          const uint32_t wb = smem_u32(sm.wbuf[seg % kBwdWBufs]);
 #pragma unroll
           for (int k = 0; k < kND / 16; ++k) {
             const uint64_t ad = smem_desc(base + kBwdXBytes + k * 32, 16, 512, 4);
@@ -235,10 +257,10 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         mma_commit(smem_u32(&sm.tfull[acc]));
         if (last_in_seg) {
           if (a.with_dw) mma_commit(smem_u32(&sm.dwfull));
-          mma_commit(smem_u32(&sm.wempty[seg & 1]));
+          mma_commit(smem_u32(&sm.wempty[seg % kBwdWBufs]));
         }
         first_in_seg = false;
-        if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+        if (++acc == kBwdAcc) { acc = 0; acc_phase ^= 1; }
         if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
       }
       mma_commit(smem_u32(&sm.mma_done));
@@ -294,23 +316,21 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       tmem_ld_32x32b_x32(tl, v[0]);
       tmem_ld_32x32b_x32(tl + 32, v[1]);
       tmem_wait_ld();
-      // Columns 64h .. 64h+63 of row r are one 128-byte row of x box h.
+      // Columns 64h .. 64h+63 of row r are one 128-byte row of x box h; read
+      // all eight 16-byte chunks before the math so the loads overlap.
       uint8_t *rowp = xs + h * kBwdXBox + r * 128;
+      uint4 xv[8];
 #pragma unroll
-      for (int j = 0; j < 2; ++j) {
+      for (int i = 0; i < 8; ++i) xv[i] = *reinterpret_cast<const uint4 *>(rowp + ((i ^ (r & 7)) << 4));
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const int chunk = (j * 4 + c) ^ (r & 7);
-          uint4 *p = reinterpret_cast<uint4 *>(rowp + chunk * 16);
-          const uint4 xv = *p;
-          const float *dv = reinterpret_cast<const float *>(v[j] + 8 * c);
-          uint4 o;
-          o.x = pack_bf16x2(fmaf(-s, bf16lo(xv.x), inv * dv[0]), fmaf(-s, bf16hi(xv.x), inv * dv[1]));
-          o.y = pack_bf16x2(fmaf(-s, bf16lo(xv.y), inv * dv[2]), fmaf(-s, bf16hi(xv.y), inv * dv[3]));
-          o.z = pack_bf16x2(fmaf(-s, bf16lo(xv.z), inv * dv[4]), fmaf(-s, bf16hi(xv.z), inv * dv[5]));
-          o.w = pack_bf16x2(fmaf(-s, bf16lo(xv.w), inv * dv[6]), fmaf(-s, bf16hi(xv.w), inv * dv[7]));
-          *p = o;
-        }
+      for (int i = 0; i < 8; ++i) {
+        const float *dv = reinterpret_cast<const float *>(v[i >> 2] + 8 * (i & 3));
+        uint4 o;
+        o.x = pack_bf16x2(fmaf(-s, bf16lo(xv[i].x), inv * dv[0]), fmaf(-s, bf16hi(xv[i].x), inv * dv[1]));
+        o.y = pack_bf16x2(fmaf(-s, bf16lo(xv[i].y), inv * dv[2]), fmaf(-s, bf16hi(xv[i].y), inv * dv[3]));
+        o.z = pack_bf16x2(fmaf(-s, bf16lo(xv[i].z), inv * dv[4]), fmaf(-s, bf16hi(xv[i].z), inv * dv[5]));
+        o.w = pack_bf16x2(fmaf(-s, bf16lo(xv[i].w), inv * dv[6]), fmaf(-s, bf16hi(xv[i].w), inv * dv[7]));
+        *reinterpret_cast<uint4 *>(rowp + ((i ^ (r & 7)) << 4)) = o;
       }
       // Every writer makes its grad_x visible to the TMA (async proxy), then
       // one arrive per warp on epi (before the TMEM release, see BwdSmem);
@@ -348,7 +368,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 #pragma unroll
         for (int d = 0; d < kND; ++d) __stcg(dst + d * kBwdBK, __uint_as_float(v[d]));
       }
-      if (++acc == 2) { acc = 0; acc_phase ^= 1; }
+      if (++acc == kBwdAcc) { acc = 0; acc_phase ^= 1; }
       if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
     }
     if (leader) {
@@ -404,28 +424,39 @@ __global__ void k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go,
 }
 
 // grad_W[d, k] = bf16(sum of the partials of every CTA whose unit range
-// touches k-chunk k / 128), in increasing CTA order.
-__global__ void k1_bwd_dw_reduce_kernel(const float *__restrict__ part,
-                                        __nv_bfloat16 *__restrict__ gW, int nC, int ntt,
-                                        int64_t units, int grid, int maxseg) {
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (i >= int64_t(kND) * nC) return;
-  const int d = int(i / nC);
-  const int k = int(i - int64_t(d) * nC);
-  const int kc = k / kBwdBK, kl = k - kc * kBwdBK;
-  const int64_t lo = int64_t(kc) * ntt, hi = lo + ntt;  // units of this k-chunk
-  int c = int(lo * grid / units) - 1;
-  if (c < 0) c = 0;
-  float acc = 0.f;
-  for (; c < grid; ++c) {
-    const int64_t c0 = int64_t(c) * units / grid, c1 = int64_t(c + 1) * units / grid;
-    if (c0 >= hi) break;
-    if (c1 <= lo || c1 <= c0) continue;
-    const int seg = kc - int(c0 / ntt);
-    if (seg < 0 || seg >= maxseg) continue;
-    acc += part[(int64_t(c) * maxseg + seg) * (kND * kBwdBK) + d * kBwdBK + kl];
+// touches k-chunk k / 128), in increasing CTA order (deterministic).
+// Block (kc, dg): k-chunk kc, rows d = 8 dg .. 8 dg + 7; the contributing
+// (CTA, segment) pairs are found once per block.
+__global__ void __launch_bounds__(256)
+k1_bwd_dw_reduce_kernel(const float *__restrict__ part, __nv_bfloat16 *__restrict__ gW, int nC,
+                        int ntt, int64_t units, int grid, int maxseg) {
+  __shared__ int contrib[kRedMaxContrib];
+  __shared__ int ncontrib;
+  const int kc = blockIdx.x, dg = blockIdx.y;
+  if (threadIdx.x == 0) {
+    const int64_t lo = int64_t(kc) * ntt, hi = lo + ntt;  // units of this k-chunk
+    int c = int(lo * grid / units) - 1;
+    if (c < 0) c = 0;
+    int n = 0;
+    for (; c < grid && n < kRedMaxContrib; ++c) {
+      const int64_t c0 = int64_t(c) * units / grid, c1 = int64_t(c + 1) * units / grid;
+      if (c0 >= hi) break;
+      if (c1 <= lo || c1 <= c0) continue;
+      const int seg = kc - int(c0 / ntt);
+      if (seg >= 0 && seg < maxseg) contrib[n++] = c * maxseg + seg;
+    }
+    ncontrib = n;
   }
-  gW[int64_t(d) * nC + k] = __float2bfloat16_rn(acc);
+  __syncthreads();
+  const int n = ncontrib;
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    const int e = threadIdx.x + 256 * i;  // 0 .. 1023: (d_local, k_local)
+    const int d = dg * 8 + (e >> 7), kl = e & 127;
+    float acc = 0.f;
+    for (int j = 0; j < n; ++j) acc += part[int64_t(contrib[j]) * (kND * kBwdBK) + d * kBwdBK + kl];
+    gW[int64_t(d) * nC + int64_t(kc) * kBwdBK + kl] = __float2bfloat16_rn(acc);
+  }
 }
 
 }  // namespace k1tc

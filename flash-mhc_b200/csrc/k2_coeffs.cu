@@ -217,13 +217,16 @@ k2_bwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
   }
 }
 
+// One warp per parameter: lane l sums blocks l, l+32, ... then a fixed
+// butterfly (deterministic).
 __global__ void k2_param_reduce_kernel(const float *__restrict__ part, float *__restrict__ g_params,
                                        int nblocks) {
-  const int i = threadIdx.x;
-  if (i >= kP) return;
+  const int i = blockIdx.x, lane = threadIdx.x;
   float s = 0.f;
-  for (int b = 0; b < nblocks; ++b) s += part[int64_t(b) * kP + i];
-  g_params[i] = s;
+  for (int b = lane; b < nblocks; b += 32) s += part[int64_t(b) * kP + i];
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
+  if (lane == 0) g_params[i] = s;
 }
 
 int64_t k2_bwd_workspace_bytes(int64_t T) {
@@ -245,7 +248,7 @@ void launch_k2_bwd(const void *proj, const float *params, const float *perm, con
   k2_bwd_kernel<<<nb, 256, 0, s>>>((const bf16 *)proj, params, perm, (const float4 *)g_hpre,
                                    (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj,
                                    ws, T);
-  k2_param_reduce_kernel<<<1, 64, 0, s>>>(ws, g_params, int(nb));
+  k2_param_reduce_kernel<<<kP, 32, 0, s>>>(ws, g_params, int(nb));
 }
 
 }  // namespace fmhc

@@ -260,7 +260,8 @@ def test_metric_shape_runs_the_tensor_core_k1():
 
 
 @pytest.mark.parametrize("T,C", [(1, 256), (31, 256), (33, 256), (1000, 256), (4733, 256),
-                                 (3000, 1024), (129, 2048)])
+                                 (3000, 1024), (129, 2048),
+                                 (65536, 64)])  # 2 k-chunks: ~74 CTAs add into each
 def test_k1_token_partitioning(T, C):
     """Forward: token ranges split across CTAs in 32-row units, partial tiles.
     Backward: (k-chunk, token-tile) unit runs per CTA that cross k-chunk
