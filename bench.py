@@ -1,6 +1,6 @@
 """Benchmark of the mHC-lite hot path on B200 (one JSON line on rank 0).
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference|reference-triton]
 
 Metric: tokens/s fwd+bwd per GPU and % HBM roofline of
 K1/K3/K4 at T=65536, C=1024, n=4 (the kernel-level microbench config).  One
@@ -30,6 +30,9 @@ all-reduced over NCCL, the path's only exchange.
   Triton-only and it has no compiled CPU implementation of this path, so the
   arm times the CPU restatement of the reference algorithm (oracle port) with
   all host cores on the same workload, rank 0 only.
+* ``--impl reference-triton``: a comparison line, not the reference arm -- the
+  unmodified reference's Triton kernels and block, installed in
+  ``baseline/_ref``, timed on this GPU on the same shapes and seeds.
 """
 
 from __future__ import annotations
@@ -170,8 +173,9 @@ class ClockSampler:
 class HotPath:
     """Inputs and the fwd+bwd step of the hot path on one GPU."""
 
-    # kernels of this library launched per step: K1 fwd, K3 fwd, K4 fwd, K4 bwd,
-    # K3 bwd, K1 bwd-dx, K1 grad_W (2: split partials + reduction)
+    # kernels of this library launched per step (8): K1 fwd, K3 fwd, K4 fwd,
+    # K4 bwd, K3 bwd, and K1 bwd as prep (gos, s/inv_rms) + the fused
+    # grad_x/grad_W kernel + the grad_W reduction
     def __init__(self, T, C, device, seed, torch):
         self.torch = torch
         self.T, self.C = T, C
@@ -621,12 +625,139 @@ def run_reference(args):
     print(json.dumps(line), flush=True)
 
 
+def run_reference_triton(args):
+    """The reference's own Triton kernels on this GPU (a comparison line).
+
+    Imports the unmodified reference from ``baseline/_ref`` (pip-installed from
+    the reference's source tree) instead of this repository's package -- both
+    are named ``flash_mhc`` -- and times (1) the same six-op step as
+    ``HotPath`` through the reference's ops, K1's weight gradient taken as the
+    reference's autograd takes it (``ops.py:683-684``: a bf16 matmul of
+    ``go * inv_rms`` with x), and (2) the reference's ``MHCLiteBlock``
+    (triton_fused, activation checkpointing) at the block config.  Rank 0 only.
+    """
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    ref_dir = ROOT / "baseline" / "_ref"
+    line = {"impl": "reference-triton", "metric": METRIC, "unit": UNIT}
+    if not (ref_dir / "flash_mhc").is_dir():
+        line["unavailable"] = "baseline/_ref holds no installed reference package"
+        print(json.dumps(line), flush=True)
+        return
+    sys.path[:] = [p for p in sys.path if Path(p).resolve() not in (ROOT, ROOT / "flash-mhc_b200")]
+    sys.path.insert(0, str(ref_dir))
+    import torch
+    import torch.nn as nn
+    import flash_mhc as ref  # the reference package
+    if ref_dir.resolve() not in Path(ref.__file__).resolve().parents:
+        raise RuntimeError(f"expected the reference from {ref_dir}, got {ref.__file__}")
+    ops = torch.ops.flash_mhc
+    dev = "cuda"
+    T, C, n, D = args.T, args.C, N_STREAMS, D_OUT
+    g = torch.Generator(device=dev)
+    g.manual_seed(1234)
+
+    def rn(*shape, std=1.0, dt=torch.bfloat16):
+        return (torch.randn(*shape, generator=g, device=dev) * std).to(dt)
+
+    x = rn(T, n, C)
+    W = rn(D, n * C, std=0.02)
+    lo = rn(T, C)
+    hp, hq, H = rn(T, n, dt=torch.float32), rn(T, n, dt=torch.float32), rn(T, n, n, dt=torch.float32)
+    gp, g3, g4 = rn(T, D), rn(T, C), rn(T, n, C)
+    xf = x.reshape(T, n * C)
+
+    def k1_bwd(proj, inv):
+        gx = ops.fused_rmsnorm_project_bwd_dx(gp, xf, W, proj, inv)
+        gW = torch.matmul((gp * inv[:, None]).to(xf.dtype).t(), xf)
+        return gx, gW
+
+    def step(ev=None):
+        def rec(k, f):
+            if ev is None:
+                return f()
+            s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            s.record()
+            r = f()
+            e.record()
+            ev.setdefault(k, []).append((s, e))
+            return r
+        proj, inv = rec("k1_fwd", lambda: ops.fused_rmsnorm_project(xf, W))
+        rec("k3_fwd", lambda: ops.fused_pre_map(x, hp))
+        rec("k4_fwd", lambda: ops.fused_post_res(x, lo, H, hq))
+        rec("k4_bwd", lambda: ops.fused_post_res_backward(g4, x, lo, H, hq))
+        rec("k3_bwd", lambda: ops.fused_pre_map_backward(g3, x, hp))
+        rec("k1_bwd", lambda: k1_bwd(proj, inv))
+
+    t_tune = time.time()
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    tune_s = time.time() - t_tune
+    s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(args.steps):
+        step()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / args.steps
+    ev = {}
+    for _ in range(5):
+        step(ev)
+    torch.cuda.synchronize()
+    kernels = {k: round(sum(a.elapsed_time(b) for a, b in v) / len(v), 4) for k, v in ev.items()}
+    line.update({
+        "value": round(T / (ms * 1e-3), 1), "n_gpus": 1, "steps": args.steps,
+        "warmup": max(args.warmup, 3), "ms_per_step": round(ms, 4), "higher_is_better": True,
+        "dtype": "bf16", "data": "synthetic (same seeds and distributions as impl ours)",
+        "config": {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
+                   "T_per_gpu": T, "C": C, "n": n, "D": D},
+        "kernels_ms": kernels,
+        "autotune": os.environ.get("FLASH_MHC_TRITON_AUTOTUNE", "default"),
+        "warmup_s_incl_autotune": round(tune_s, 1),
+        "source": "unmodified reference installed in baseline/_ref, torch.ops.flash_mhc (Triton)",
+    })
+    del x, W, lo, hp, hq, H, gp, g3, g4, xf
+    if not args.no_block:
+        Tb, Cb = args.block_T, args.block_C
+        layer = nn.Linear(Cb, Cb, bias=False)
+        blk = ref.MHCLiteBlock(n, Cb, layer, triton_fused=True, activation_checkpointing=True)
+        blk = blk.to(dev).to(torch.bfloat16).train()
+        with torch.no_grad():
+            layer.weight.copy_(rn(Cb, Cb, std=0.02))
+        xb = rn(Tb, n, Cb).requires_grad_(True)
+        up = rn(Tb, n, Cb)
+
+        def bstep():
+            blk.zero_grad(set_to_none=True)
+            xb.grad = None
+            blk(xb).backward(up)
+
+        for _ in range(3):
+            bstep()
+        torch.cuda.synchronize()
+        s.record()
+        for _ in range(10):
+            bstep()
+        e.record()
+        torch.cuda.synchronize()
+        bms = s.elapsed_time(e) / 10
+        line["block"] = {"config": {"workload": "MHCLiteBlock fwd+bwd, activation checkpointing "
+                                                "(configs[2])", "T_per_gpu": Tb, "C": Cb, "n": n},
+                         "value": round(Tb / (bms * 1e-3), 1), "unit": UNIT,
+                         "ms_per_step": round(bms, 4), "steps": 10}
+    print(json.dumps(line), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=20)
     ap.add_argument("--warmup", type=int, default=5)
-    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--impl", choices=["ours", "reference", "reference-triton"], default="ours",
+                    help="reference: the CPU reference arm; reference-triton: the reference's "
+                         "own Triton kernels on this GPU from baseline/_ref (comparison line)")
     ap.add_argument("--T", type=int, default=65536, help="tokens per GPU")
     ap.add_argument("--C", type=int, default=1024)
     ap.add_argument("--cpu-tokens-per-worker", type=int, default=1024)
@@ -642,6 +773,8 @@ def main():
         print("note: the timing rules ask for >= 3 warm-up steps", file=sys.stderr)
     if args.impl == "reference":
         run_reference(args)
+    elif args.impl == "reference-triton":
+        run_reference_triton(args)
     else:
         run_ours(args)
 
