@@ -425,7 +425,6 @@ BwdPlan bwd_plan(int64_t T, int64_t nC) {
   p.units = int64_t(p.nkc) * p.ntt;
   int64_t g = int64_t(device_sms()) * FMHC_K1B_CTAS_PER_SM;
   if (g > p.units) g = p.units;
-  if (g > kRedMaxContrib) g = kRedMaxContrib;  // every contributor must fit the reduce table
   if (g < 1) g = 1;
   p.grid = int(g);
   p.maxseg = 1;
@@ -496,7 +495,7 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   }
   if (with_dw) {
     const int64_t T_pad = int64_t(p.ntt) * kBwdBT;
-    k1_bwd_prep_kernel<<<unsigned((T_pad + 255) / 256), 256, 0, s>>>(
+    k1_bwd_prep_kernel<<<unsigned(T_pad / 64), 256, 0, s>>>(  // 4 threads per token
         static_cast<const __nv_bfloat16 *>(go), static_cast<const __nv_bfloat16 *>(proj), inv_rms,
         reinterpret_cast<__nv_bfloat16 *>(gos), sinv, T, T_pad, nC);
   }
@@ -516,7 +515,7 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.with_dw = with_dw ? 1 : 0;
   k1_bwd_tc_kernel<<<unsigned(p.grid), kBwdThreads, smem, s>>>(mx, mgx, mgo, mgos, mw, args);
   if (with_dw) {
-    k1_bwd_dw_reduce_kernel<<<dim3(unsigned(p.nkc), kND / 8), 256, 0, s>>>(
+    k1_bwd_dw_reduce_kernel<<<dim3(unsigned(p.nkc), kND), kBwdBK, 0, s>>>(
         part, static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.units, p.grid, p.maxseg);
   }
   return 0;

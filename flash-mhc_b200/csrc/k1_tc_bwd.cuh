@@ -21,9 +21,12 @@
 //                        2 x M128 N128 K16 into one of two TMEM buffers.
 //   warps 2-9  epilogue, two warps per TMEM lane quarter: thread = token row,
 //              warps 2-5 columns 0-63, warps 6-9 columns 64-127 of the unit:
-//              grad_x = inv*D1 - s*x written over x in the stage buffer, then
-//              stored by TMA; at a segment end warps 2-5 move the grad_W
-//              partial D2 (thread per k row) to the workspace.
+//              grad_x = inv*D1 - s*x written over x in the stage buffer; at a
+//              segment end warps 2-5 move the grad_W partial D2 (thread per
+//              k row) to the workspace.
+//   warp 10    store: TMA-stores each unit's grad_x from its stage and frees
+//              the stage as soon as the store has read it, so a stage is held
+//              only for its load, its epilogue and its store read.
 // A prep kernel computes per token s and inv_rms (float2) and the grad_W
 // operand gos; the producer brings the unit's 128 (s, inv) pairs into the
 // stage with a bulk copy, so the epilogue reads them from shared memory.  A
@@ -58,9 +61,9 @@ constexpr int kBwdXBox = kBwdBT * 64 * 2;         // 16 KiB
 constexpr int kBwdGBytes = kBwdBT * kND * 2;      // 8 KiB  (go or gos tile)
 constexpr int kBwdSBytes = kBwdBT * 8;            // 1 KiB  ((s, inv_rms) per token)
 constexpr int kBwdStageBytes = kBwdXBytes + 2 * kBwdGBytes + kBwdSBytes;  // 49 KiB
-constexpr int kBwdThreads = 320;                  // producer, MMA, 8 epilogue warps
+constexpr int kBwdThreads = 352;                  // producer, MMA, 8 epilogue warps, store
 constexpr int kBwdEpiWarps = 8;
-constexpr int kRedMaxContrib = 1024;              // >= grid (bwd_plan clamps the grid to it)
+constexpr int kBwdStoreWarp = 2 + kBwdEpiWarps;
 constexpr int kBwdWBytes = kND * kBwdBK * 2;      // 8 KiB  (two 4 KiB boxes)
 // kBwdAcc x 128 (grad_x) + 32 (grad_W) columns, rounded up to a power of two.
 constexpr uint32_t kBwdTmemCols = kBwdAcc == 2 ? 512 : 256;
@@ -77,12 +80,11 @@ struct alignas(1024) BwdSmem {
   uint64_t wempty[kBwdWBufs];
   uint64_t dwfull;
   uint64_t dwempty;
-  // epi[i & 1]: the 4 epilogue warps finished writing grad_x of local unit i.
-  // Two barriers, and each warp arrives on it before it releases the unit's
-  // TMEM accumulator: a warp can then never arrive for unit i + 2 before every
-  // warp arrived for unit i (unit i + 2 needs that accumulator back), so each
-  // phase counts exactly the four arrivals of one unit.
-  uint64_t epi[2];
+  // epi[s]: the 8 epilogue warps finished writing grad_x into stage s.  One
+  // barrier per stage: its next phase belongs to the next unit in that stage,
+  // which cannot be loaded before the store warp has waited on this phase and
+  // freed the stage, so phases never alias and each counts one unit's arrivals.
+  uint64_t epi[kBwdStages];
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
@@ -113,6 +115,19 @@ __device__ __forceinline__ void bwd_unit(int64_t u, int ntt, int &kc, int &tt) {
   tt = int(u - int64_t(kc) * ntt);
 }
 
+// Partial dot product of one 16-byte chunk (8 of the 32 d) of go and proj.
+// The full dot product is (p0 + p1) + (p2 + p3) over the four chunks, in this
+// order in both places that compute it (prep kernel, no-workspace epilogue),
+// so grad_x is identical whichever entry point computed it.
+__device__ __forceinline__ float go_proj_chunk_dot(const uint4 g, const uint4 p) {
+  float dot = 0.f;
+  dot = fmaf(bf16lo(g.x), bf16lo(p.x), dot); dot = fmaf(bf16hi(g.x), bf16hi(p.x), dot);
+  dot = fmaf(bf16lo(g.y), bf16lo(p.y), dot); dot = fmaf(bf16hi(g.y), bf16hi(p.y), dot);
+  dot = fmaf(bf16lo(g.z), bf16lo(p.z), dot); dot = fmaf(bf16hi(g.z), bf16hi(p.z), dot);
+  dot = fmaf(bf16lo(g.w), bf16lo(p.w), dot); dot = fmaf(bf16hi(g.w), bf16hi(p.w), dot);
+  return dot;
+}
+
 __global__ void __launch_bounds__(kBwdThreads, FMHC_K1B_CTAS_PER_SM)
 k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_gx,
@@ -132,7 +147,8 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   if (threadIdx.x == 0) {
     for (int s = 0; s < kBwdStages; ++s) {
       mbar_init(smem_u32(&sm.full[s]), 1);
-      mbar_init(smem_u32(&sm.empty[s]), 1);  // released by the epilogue after its store read
+      mbar_init(smem_u32(&sm.empty[s]), 1);  // released by the store warp after its store read
+      mbar_init(smem_u32(&sm.epi[s]), kBwdEpiWarps);
     }
     for (int b = 0; b < kBwdAcc; ++b) {
       mbar_init(smem_u32(&sm.tfull[b]), 1);
@@ -144,8 +160,6 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
     mbar_init(smem_u32(&sm.dwfull), 1);
     mbar_init(smem_u32(&sm.dwempty), 4);  // warps 2-5 read the grad_W partial
-    mbar_init(smem_u32(&sm.epi[0]), kBwdEpiWarps);
-    mbar_init(smem_u32(&sm.epi[1]), kBwdEpiWarps);
     mbar_init(smem_u32(&sm.mma_done), 1);
     sm.abort = 0;
     fence_mbar_init();
@@ -266,17 +280,14 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       mma_commit(smem_u32(&sm.mma_done));
       mbar_wait(smem_u32(&sm.mma_done), 0, abort, kSiteBDrain, true);
     }
-  } else {
+  } else if (warp < kBwdStoreWarp) {
     // ------------------------------------------------------------ epilogue
     const int q = warp & 3;           // TMEM lane quarter
     const int h = (warp - 2) >> 2;    // column half of the unit (0: 0-63, 1: 64-127)
     const int r = q * 32 + lane;      // token row of the unit / k row of the grad_W partial
-    const bool leader = (warp == 2 && lane == 0);
-    int stage = 0, acc = 0, seg = -1, kc_prev = -1, prev_stage = -1;
+    int stage = 0, acc = 0, seg = -1, kc_prev = -1;
     uint32_t phase = 0, acc_phase = 0;
     for (int64_t u = u0; u < u1 && !*abort; ++u) {
-      const int64_t li = u - u0;  // local unit index
-      const uint32_t epi_bar = smem_u32(&sm.epi[li & 1]);
       int kc, tt;
       bwd_unit(u, a.ntt, kc, tt);
       if (kc != kc_prev) { ++seg; kc_prev = kc; }
@@ -291,15 +302,10 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         inv = a.inv_rms[t];
         const uint4 *g4 = reinterpret_cast<const uint4 *>(a.go + t * kND);
         const uint4 *p4 = reinterpret_cast<const uint4 *>(a.proj + t * kND);
-        float dot = 0.f;
+        float pc[4];
 #pragma unroll
-        for (int c = 0; c < 4; ++c) {
-          const uint4 g = __ldg(g4 + c), p = __ldg(p4 + c);
-          dot = fmaf(bf16lo(g.x), bf16lo(p.x), dot); dot = fmaf(bf16hi(g.x), bf16hi(p.x), dot);
-          dot = fmaf(bf16lo(g.y), bf16lo(p.y), dot); dot = fmaf(bf16hi(g.y), bf16hi(p.y), dot);
-          dot = fmaf(bf16lo(g.z), bf16lo(p.z), dot); dot = fmaf(bf16hi(g.z), bf16hi(p.z), dot);
-          dot = fmaf(bf16lo(g.w), bf16lo(p.w), dot); dot = fmaf(bf16hi(g.w), bf16hi(p.w), dot);
-        }
+        for (int c = 0; c < 4; ++c) pc[c] = go_proj_chunk_dot(__ldg(g4 + c), __ldg(p4 + c));
+        const float dot = (pc[0] + pc[1]) + (pc[2] + pc[3]);
         s = dot * (inv * inv) / float(a.nC);
       }
       if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteBEpiFull)) break;
@@ -333,25 +339,13 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         *reinterpret_cast<uint4 *>(rowp + ((i ^ (r & 7)) << 4)) = o;
       }
       // Every writer makes its grad_x visible to the TMA (async proxy), then
-      // one arrive per warp on epi (before the TMEM release, see BwdSmem);
-      // only the store-issuing thread waits (bounded).
+      // one arrive per warp on epi[stage] for the store warp and on tempty.
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) {
-        mbar_arrive(epi_bar);
+        mbar_arrive(smem_u32(&sm.epi[stage]));
         mbar_arrive(smem_u32(&sm.tempty[acc]));
-      }
-      if (leader) {
-        if (!mbar_wait(epi_bar, uint32_t(li >> 1) & 1u, abort, kSiteBEpiStore)) break;
-        const uint32_t base = smem_u32(xs);
-        tma_store_2d(&tmap_gx, base, kc * kBwdBK, tt * kBwdBT);
-        tma_store_2d(&tmap_gx, base + kBwdXBox, kc * kBwdBK + 64, tt * kBwdBT);
-        tma_store_commit();
-        // The previous unit's store has finished reading its stage: release it.
-        tma_store_wait_read<1>();
-        if (prev_stage >= 0) mbar_arrive(smem_u32(&sm.empty[prev_stage]));
-        prev_stage = stage;
       }
       if (a.with_dw && last_in_seg && h == 0) {
         // grad_W partial of this segment: thread r owns k row r, 32 d columns.
@@ -371,9 +365,26 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       if (++acc == kBwdAcc) { acc = 0; acc_phase ^= 1; }
       if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
     }
-    if (leader) {
+  } else {
+    // --------------------------------------------------------------- store
+    if (lane == 0) {
+      int stage = 0;
+      uint32_t phase = 0;
+      for (int64_t u = u0; u < u1 && !*abort; ++u) {
+        int kc, tt;
+        bwd_unit(u, a.ntt, kc, tt);
+        if (!mbar_wait(smem_u32(&sm.epi[stage]), phase, abort, kSiteBEpiStore)) break;
+        const uint32_t base = smem_u32(sm.stage[stage]);
+        tma_store_2d(&tmap_gx, base, kc * kBwdBK, tt * kBwdBT);
+        tma_store_2d(&tmap_gx, base + kBwdXBox, kc * kBwdBK + 64, tt * kBwdBT);
+        tma_store_commit();
+        // Free the stage once this store has read it (the global writes may
+        // still be in flight).
+        tma_store_wait_read<0>();
+        mbar_arrive(smem_u32(&sm.empty[stage]));
+        if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
+      }
       tma_store_wait_all<0>();
-      if (prev_stage >= 0) mbar_arrive(smem_u32(&sm.empty[prev_stage]));
     }
   }
 
@@ -388,75 +399,72 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 // Per token: sinv[t] = (s, inv_rms) with s = (go . proj) * inv_rms^2 / nC,
 // and (when gos != nullptr) gos[t, :] = bf16(go[t, :] * inv_rms[t]), the
 // grad_W operand, rounded like the reference's (grad_out * inv_rms).to(x.dtype).
-// One thread per token; rows T .. T_pad-1 of sinv are zeroed.
-__global__ void k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go,
-                                   const __nv_bfloat16 *__restrict__ proj,
-                                   const float *__restrict__ inv_rms,
-                                   __nv_bfloat16 *__restrict__ gos, float2 *__restrict__ sinv,
-                                   int64_t T, int64_t T_pad, int nC) {
-  const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= T_pad) return;
-  if (t >= T) {
-    sinv[t] = make_float2(0.f, 0.f);
-    return;
+// Four threads per token, one 16-byte chunk of go and proj each; the chunk
+// dot products are combined with two shuffles.  Rows T .. T_pad-1 of sinv
+// are zeroed.  The grid covers exactly 4 * T_pad threads (T_pad is a multiple
+// of 128), so every warp is whole.
+__global__ void __launch_bounds__(256)
+k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go, const __nv_bfloat16 *__restrict__ proj,
+                   const float *__restrict__ inv_rms, __nv_bfloat16 *__restrict__ gos,
+                   float2 *__restrict__ sinv, int64_t T, int64_t T_pad, int nC) {
+  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
+  const int64_t t = i >> 2;
+  const int c = int(i & 3);
+  if (t >= T_pad) return;  // never splits a warp (see above)
+  const bool valid = t < T;
+  float r = 0.f, dot = 0.f;
+  uint4 g = make_uint4(0, 0, 0, 0);
+  if (valid) {
+    r = inv_rms[t];
+    g = __ldg(reinterpret_cast<const uint4 *>(go + t * kND) + c);
+    const uint4 p = __ldg(reinterpret_cast<const uint4 *>(proj + t * kND) + c);
+    dot = go_proj_chunk_dot(g, p);
   }
-  const float r = inv_rms[t];
-  const uint4 *g4 = reinterpret_cast<const uint4 *>(go + t * kND);
-  const uint4 *p4 = reinterpret_cast<const uint4 *>(proj + t * kND);
-  float dot = 0.f;
-#pragma unroll
-  for (int c = 0; c < 4; ++c) {
-    const uint4 g = __ldg(g4 + c), p = __ldg(p4 + c);
-    dot = fmaf(bf16lo(g.x), bf16lo(p.x), dot); dot = fmaf(bf16hi(g.x), bf16hi(p.x), dot);
-    dot = fmaf(bf16lo(g.y), bf16lo(p.y), dot); dot = fmaf(bf16hi(g.y), bf16hi(p.y), dot);
-    dot = fmaf(bf16lo(g.z), bf16lo(p.z), dot); dot = fmaf(bf16hi(g.z), bf16hi(p.z), dot);
-    dot = fmaf(bf16lo(g.w), bf16lo(p.w), dot); dot = fmaf(bf16hi(g.w), bf16hi(p.w), dot);
-    if (gos) {
-      uint4 o;
-      o.x = pack_bf16x2(bf16lo(g.x) * r, bf16hi(g.x) * r);
-      o.y = pack_bf16x2(bf16lo(g.y) * r, bf16hi(g.y) * r);
-      o.z = pack_bf16x2(bf16lo(g.z) * r, bf16hi(g.z) * r);
-      o.w = pack_bf16x2(bf16lo(g.w) * r, bf16hi(g.w) * r);
-      reinterpret_cast<uint4 *>(gos + t * kND)[c] = o;
-    }
+  dot += __shfl_xor_sync(0xffffffffu, dot, 1);
+  dot += __shfl_xor_sync(0xffffffffu, dot, 2);
+  if (valid && gos) {
+    uint4 o;
+    o.x = pack_bf16x2(bf16lo(g.x) * r, bf16hi(g.x) * r);
+    o.y = pack_bf16x2(bf16lo(g.y) * r, bf16hi(g.y) * r);
+    o.z = pack_bf16x2(bf16lo(g.z) * r, bf16hi(g.z) * r);
+    o.w = pack_bf16x2(bf16lo(g.w) * r, bf16hi(g.w) * r);
+    reinterpret_cast<uint4 *>(gos + t * kND)[c] = o;
   }
-  sinv[t] = make_float2(dot * (r * r) / float(nC), r);
+  if (c == 0) sinv[t] = valid ? make_float2(dot * (r * r) / float(nC), r) : make_float2(0.f, 0.f);
 }
 
 // grad_W[d, k] = bf16(sum of the partials of every CTA whose unit range
 // touches k-chunk k / 128), in increasing CTA order (deterministic).
-// Block (kc, dg): k-chunk kc, rows d = 8 dg .. 8 dg + 7; the contributing
-// (CTA, segment) pairs are found once per block.
-__global__ void __launch_bounds__(256)
+// Block (kc, d): row d of k-chunk kc, one thread per column.  CTA c owns units
+// [c*units/grid, (c+1)*units/grid) and grid <= units, so no CTA is empty and
+// the contributors of the chunk's units [lo, hi) are exactly the CTAs from the
+// owner of lo to the owner of hi - 1, where owner(u) = ((u+1)*grid - 1) / units.
+// Their partials are loaded eight at a time and added in CTA order.
+__global__ void __launch_bounds__(kBwdBK)
 k1_bwd_dw_reduce_kernel(const float *__restrict__ part, __nv_bfloat16 *__restrict__ gW, int nC,
                         int ntt, int64_t units, int grid, int maxseg) {
-  __shared__ int contrib[kRedMaxContrib];
-  __shared__ int ncontrib;
-  const int kc = blockIdx.x, dg = blockIdx.y;
-  if (threadIdx.x == 0) {
-    const int64_t lo = int64_t(kc) * ntt, hi = lo + ntt;  // units of this k-chunk
-    int c = int(lo * grid / units) - 1;
-    if (c < 0) c = 0;
-    int n = 0;
-    for (; c < grid && n < kRedMaxContrib; ++c) {
-      const int64_t c0 = int64_t(c) * units / grid, c1 = int64_t(c + 1) * units / grid;
-      if (c0 >= hi) break;
-      if (c1 <= lo || c1 <= c0) continue;
-      const int seg = kc - int(c0 / ntt);
-      if (seg >= 0 && seg < maxseg) contrib[n++] = c * maxseg + seg;
-    }
-    ncontrib = n;
-  }
-  __syncthreads();
-  const int n = ncontrib;
+  const int kc = blockIdx.x, d = blockIdx.y, kl = threadIdx.x;
+  const int64_t lo = int64_t(kc) * ntt, hi = lo + ntt;
+  const int c_first = int(((lo + 1) * grid - 1) / units);
+  const int c_last = int((hi * grid - 1) / units);
+  const float *col = part + int64_t(d) * kBwdBK + kl;
+  float acc = 0.f;
+  for (int c = c_first; c <= c_last; c += 8) {
+    float v[8];
 #pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    const int e = threadIdx.x + 256 * i;  // 0 .. 1023: (d_local, k_local)
-    const int d = dg * 8 + (e >> 7), kl = e & 127;
-    float acc = 0.f;
-    for (int j = 0; j < n; ++j) acc += part[int64_t(contrib[j]) * (kND * kBwdBK) + d * kBwdBK + kl];
-    gW[int64_t(d) * nC + int64_t(kc) * kBwdBK + kl] = __float2bfloat16_rn(acc);
+    for (int i = 0; i < 8; ++i) {
+      const int cc = c + i;
+      v[i] = 0.f;
+      if (cc <= c_last) {
+        const int seg = kc - int((int64_t(cc) * units / grid) / ntt);
+        v[i] = __ldg(col + (int64_t(cc) * maxseg + seg) * (kND * kBwdBK));
+      }
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      if (c + i <= c_last) acc += v[i];
   }
+  gW[int64_t(d) * nC + int64_t(kc) * kBwdBK + kl] = __float2bfloat16_rn(acc);
 }
 
 }  // namespace k1tc
