@@ -5,10 +5,54 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include <cstdlib>
+#include <utility>
+
 namespace fmhc {
 
 constexpr int kStreams = 4;   // n: residual streams (the kernels are specialised for 4)
 constexpr int kWarp = 32;
+
+// ---------------------------------------------------------------------------
+// Programmatic dependent launch.  Every kernel of this library is launched
+// with launch() below, so the next kernel in the stream is scheduled as the
+// CTAs of the previous one exit instead of after the whole grid has drained
+// and flushed, hiding launch latency and the next kernel's prologue (barrier
+// set-up, TMEM allocation, tensor-map prefetch).  The rule that makes this
+// safe: every kernel calls pdl_wait() before its first global-memory access
+// (read or write); it returns once the preceding grid has completed and its
+// writes are visible.  No kernel triggers its dependents early: a trigger at
+// kernel start let the whole step's kernels launch ahead and park CTAs on the
+// SMs, 17% slower than none; without it a dependent cannot become resident
+// beside a CTA of its predecessor, so TMEM and shared memory are never
+// contended across kernels.
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+
+// On unless the environment sets FLASH_MHC_PDL=0 (read once per process).
+inline bool pdl_enabled() {
+  static const bool on = [] {
+    const char *e = std::getenv("FLASH_MHC_PDL");
+    return !(e != nullptr && e[0] == '0');
+  }();
+  return on;
+}
+
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch(void (*kernel)(KArgs...), dim3 grid, dim3 block, size_t smem,
+                          cudaStream_t s, Args &&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = s;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = pdl_enabled() ? 1 : 0;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kernel, std::forward<Args>(args)...);
+}
 
 // ---------------------------------------------------------------------------
 // bf16 <-> f32 on packed 32-bit words.  bf16 -> f32 is exact (a shift);

@@ -26,6 +26,7 @@ __global__ void __launch_bounds__(256)
 k1_fwd_simt_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
                    bf16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T, int nC,
                    int D) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -75,6 +76,7 @@ k1_bwd_dx_simt_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
                       const bf16 *__restrict__ W, const bf16 *__restrict__ proj,
                       const float *__restrict__ inv_rms, bf16 *__restrict__ gx, int64_t T,
                       int nC, int D) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -132,6 +134,7 @@ __global__ void __launch_bounds__(256)
 k1_dw_partial_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
                      const float *__restrict__ inv_rms, float *__restrict__ ws, int64_t T,
                      int nC, int D, int64_t tokens_per_split) {
+  pdl_wait();
   __shared__ float gos[kDwTile][32];
   const int k = blockIdx.x * 256 + threadIdx.x;
   const int split = blockIdx.y;
@@ -170,6 +173,7 @@ k1_dw_partial_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
 
 __global__ void k1_dw_reduce_kernel(const float *__restrict__ ws, bf16 *__restrict__ gW,
                                     int nsplit, int64_t n) {
+  pdl_wait();
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= n) return;
   float s = 0.f;
@@ -209,24 +213,22 @@ int warp_grid(int64_t T) {
 void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
                         int nC, int D, int vec, cudaStream_t s) {
   if (vec == 8)
-    k1_fwd_simt_kernel<8><<<warp_grid(T), 256, 0, s>>>((const bf16 *)x, (const bf16 *)W,
-                                                       (bf16 *)out, inv_rms, T, nC, D);
+    launch(k1_fwd_simt_kernel<8>, dim3(warp_grid(T)), dim3(256), 0, s, (const bf16 *)x,
+           (const bf16 *)W, (bf16 *)out, inv_rms, T, nC, D);
   else
-    k1_fwd_simt_kernel<1><<<warp_grid(T), 256, 0, s>>>((const bf16 *)x, (const bf16 *)W,
-                                                       (bf16 *)out, inv_rms, T, nC, D);
+    launch(k1_fwd_simt_kernel<1>, dim3(warp_grid(T)), dim3(256), 0, s, (const bf16 *)x,
+           (const bf16 *)W, (bf16 *)out, inv_rms, T, nC, D);
 }
 
 void launch_k1_bwd_dx_simt(const void *go, const void *x, const void *W, const void *proj,
                            const float *inv_rms, void *gx, int64_t T, int nC, int D, int vec,
                            cudaStream_t s) {
   if (vec == 8)
-    k1_bwd_dx_simt_kernel<8><<<warp_grid(T), 256, 0, s>>>(
-        (const bf16 *)go, (const bf16 *)x, (const bf16 *)W, (const bf16 *)proj, inv_rms,
-        (bf16 *)gx, T, nC, D);
+    launch(k1_bwd_dx_simt_kernel<8>, dim3(warp_grid(T)), dim3(256), 0, s, (const bf16 *)go,
+           (const bf16 *)x, (const bf16 *)W, (const bf16 *)proj, inv_rms, (bf16 *)gx, T, nC, D);
   else
-    k1_bwd_dx_simt_kernel<1><<<warp_grid(T), 256, 0, s>>>(
-        (const bf16 *)go, (const bf16 *)x, (const bf16 *)W, (const bf16 *)proj, inv_rms,
-        (bf16 *)gx, T, nC, D);
+    launch(k1_bwd_dx_simt_kernel<1>, dim3(warp_grid(T)), dim3(256), 0, s, (const bf16 *)go,
+           (const bf16 *)x, (const bf16 *)W, (const bf16 *)proj, inv_rms, (bf16 *)gx, T, nC, D);
 }
 
 void launch_k1_dw_simt(const void *go, const void *x, const float *inv_rms, void *gW,
@@ -234,10 +236,11 @@ void launch_k1_dw_simt(const void *go, const void *x, const float *inv_rms, void
   const int nsplit = k1_dw_splits(T);
   const int64_t per = (T + nsplit - 1) / nsplit;
   dim3 grid((nC + 255) / 256, nsplit);
-  k1_dw_partial_kernel<<<grid, 256, 0, s>>>((const bf16 *)go, (const bf16 *)x, inv_rms, ws, T,
-                                            nC, D, per);
+  launch(k1_dw_partial_kernel, dim3(grid), dim3(256), 0, s, (const bf16 *)go, (const bf16 *)x,
+         inv_rms, ws, T, nC, D, per);
   const int64_t n = int64_t(D) * nC;
-  k1_dw_reduce_kernel<<<int((n + 255) / 256), 256, 0, s>>>(ws, (bf16 *)gW, nsplit, n);
+  launch(k1_dw_reduce_kernel, dim3(int((n + 255) / 256)), dim3(256), 0, s, ws, (bf16 *)gW, nsplit,
+         n);
 }
 
 }  // namespace fmhc

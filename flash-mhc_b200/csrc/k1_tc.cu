@@ -132,6 +132,8 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // No global memory is touched before this point (see pdl_wait()).
+  pdl_wait();
 
   if (warp == 0) {
     // ---------------------------------------------------------- producer
@@ -401,8 +403,8 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
   if (grid > units) grid = units;
   const size_t smem = sizeof(FwdSmem) + 1024;
   if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_kernel), smem)) return e;
-  k1_fwd_tc_kernel<<<unsigned(grid), kThreads, smem, s>>>(
-      mx, mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units);
+  launch(k1_fwd_tc_kernel, dim3(unsigned(grid)), dim3(kThreads), smem, s, mx, mw,
+         reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units);
   return 0;
 }
 
@@ -495,9 +497,10 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   }
   if (with_dw) {
     const int64_t T_pad = int64_t(p.ntt) * kBwdBT;
-    k1_bwd_prep_kernel<<<unsigned(T_pad / 64), 256, 0, s>>>(  // 4 threads per token
-        static_cast<const __nv_bfloat16 *>(go), static_cast<const __nv_bfloat16 *>(proj), inv_rms,
-        reinterpret_cast<__nv_bfloat16 *>(gos), sinv, T, T_pad, nC);
+    // 4 threads per token
+    launch(k1_bwd_prep_kernel, dim3(unsigned(T_pad / 64)), dim3(256), 0, s,
+           static_cast<const __nv_bfloat16 *>(go), static_cast<const __nv_bfloat16 *>(proj),
+           inv_rms, reinterpret_cast<__nv_bfloat16 *>(gos), sinv, T, T_pad, nC);
   }
   const size_t smem = sizeof(BwdSmem) + 1024;
   if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_bwd_tc_kernel), smem)) return e;
@@ -513,10 +516,11 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.units = p.units;
   args.maxseg = p.maxseg;
   args.with_dw = with_dw ? 1 : 0;
-  k1_bwd_tc_kernel<<<unsigned(p.grid), kBwdThreads, smem, s>>>(mx, mgx, mgo, mgos, mw, args);
+  launch(k1_bwd_tc_kernel, dim3(unsigned(p.grid)), dim3(kBwdThreads), smem, s, mx, mgx, mgo, mgos,
+         mw, args);
   if (with_dw) {
-    k1_bwd_dw_reduce_kernel<<<dim3(unsigned(p.nkc), kND), kBwdBK, 0, s>>>(
-        part, static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.units, p.grid, p.maxseg);
+    launch(k1_bwd_dw_reduce_kernel, dim3(unsigned(p.nkc), kND), dim3(kBwdBK), 0, s, part,
+           static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.units, p.grid, p.maxseg);
   }
   return 0;
 }

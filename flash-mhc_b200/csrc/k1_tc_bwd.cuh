@@ -177,6 +177,8 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = sm.tmem_base;
+  // No global memory is touched before this point (see pdl_wait()).
+  pdl_wait();
 
   if (warp == 0) {
     // ------------------------------------------------------------ producer
@@ -407,6 +409,7 @@ __global__ void __launch_bounds__(256)
 k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go, const __nv_bfloat16 *__restrict__ proj,
                    const float *__restrict__ inv_rms, __nv_bfloat16 *__restrict__ gos,
                    float2 *__restrict__ sinv, int64_t T, int64_t T_pad, int nC) {
+  pdl_wait();
   const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   const int64_t t = i >> 2;
   const int c = int(i & 3);
@@ -443,6 +446,7 @@ k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go, const __nv_bfloat16 *__
 __global__ void __launch_bounds__(kBwdBK)
 k1_bwd_dw_reduce_kernel(const float *__restrict__ part, __nv_bfloat16 *__restrict__ gW, int nC,
                         int ntt, int64_t units, int grid, int maxseg) {
+  pdl_wait();
   const int kc = blockIdx.x, d = blockIdx.y, kl = threadIdx.x;
   const int64_t lo = int64_t(kc) * ntt, hi = lo + ntt;
   const int c_first = int(((lo + 1) * grid - 1) / units);

@@ -98,6 +98,7 @@ __global__ void __launch_bounds__(256)
 k2_fwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
               const float *__restrict__ perm, float4 *__restrict__ h_pre,
               float4 *__restrict__ h_post, float4 *__restrict__ H, int64_t T) {
+  pdl_wait();
   __shared__ K2Smem sm;
   load_params(sm, params, perm);
   const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
@@ -128,6 +129,7 @@ k2_bwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
               const float *__restrict__ perm, const float4 *__restrict__ g_hpre,
               const float4 *__restrict__ g_hpost, const float4 *__restrict__ g_H,
               bf16 *__restrict__ g_proj, float *__restrict__ part, int64_t T) {
+  pdl_wait();
   __shared__ K2Smem sm;
   __shared__ float red[8][kP];
   load_params(sm, params, perm);
@@ -221,6 +223,7 @@ k2_bwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
 // butterfly (deterministic).
 __global__ void k2_param_reduce_kernel(const float *__restrict__ part, float *__restrict__ g_params,
                                        int nblocks) {
+  pdl_wait();
   const int i = blockIdx.x, lane = threadIdx.x;
   float s = 0.f;
   for (int b = lane; b < nblocks; b += 32) s += part[int64_t(b) * kP + i];
@@ -237,18 +240,18 @@ int64_t k2_bwd_workspace_bytes(int64_t T) {
 void launch_k2_fwd(const void *proj, const float *params, const float *perm, float *h_pre,
                    float *h_post, float *H, int64_t T, cudaStream_t s) {
   const unsigned nb = unsigned((T + 255) / 256);
-  k2_fwd_kernel<<<nb, 256, 0, s>>>((const bf16 *)proj, params, perm, (float4 *)h_pre,
-                                   (float4 *)h_post, (float4 *)H, T);
+  launch(k2_fwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj, params, perm,
+         (float4 *)h_pre, (float4 *)h_post, (float4 *)H, T);
 }
 
 void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
                    const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
                    float *ws, int64_t T, cudaStream_t s) {
   const unsigned nb = unsigned((T + 255) / 256);
-  k2_bwd_kernel<<<nb, 256, 0, s>>>((const bf16 *)proj, params, perm, (const float4 *)g_hpre,
-                                   (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj,
-                                   ws, T);
-  k2_param_reduce_kernel<<<kP, 32, 0, s>>>(ws, g_params, int(nb));
+  launch(k2_bwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj, params, perm,
+         (const float4 *)g_hpre, (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj, ws,
+         T);
+  launch(k2_param_reduce_kernel, dim3(kP), dim3(32), 0, s, ws, g_params, int(nb));
 }
 
 }  // namespace fmhc

@@ -54,6 +54,7 @@ template <int VEC, int U, int MINB>
 __global__ void __launch_bounds__(256, MINB)
 k3_fwd_kernel(const bf16 *__restrict__ x, const float4 *__restrict__ hp,
               bf16 *__restrict__ out, int64_t T, int C) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -98,6 +99,7 @@ __global__ void __launch_bounds__(256, MINB)
 k3_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const float4 *__restrict__ hp, bf16 *__restrict__ gx,
               float *__restrict__ gh, int64_t T, int C) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -151,6 +153,7 @@ __global__ void __launch_bounds__(256, MINB)
 k4_fwd_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ lo,
               const float4 *__restrict__ H, const float4 *__restrict__ hpost,
               bf16 *__restrict__ out, int64_t T, int C) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -214,6 +217,7 @@ k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const float4 *__restrict__ hpost, bf16 *__restrict__ gx,
               bf16 *__restrict__ glo, float *__restrict__ gH,
               float *__restrict__ ghp, int64_t T, int C) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -306,6 +310,7 @@ __global__ void __launch_bounds__(256)
 grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli,
                       const float4 *__restrict__ hp, const bf16 *__restrict__ gx4,
                       bf16 *__restrict__ gx, int64_t T, int C) {
+  pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
@@ -408,8 +413,8 @@ void launch_k3_fwd(const void *x, const float *hp, void *out, int64_t T, int C, 
                    cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
     auto k = k3_fwd_kernel<VEC, FMHC_K3F_U, FMHC_K3F_MINB>;
-    k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
-        (const bf16 *)x, (const float4 *)hp, (bf16 *)out, T, C);
+    launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)x,
+           (const float4 *)hp, (bf16 *)out, T, C);
   });
 }
 
@@ -417,8 +422,8 @@ void launch_k3_bwd(const void *go, const void *x, const float *hp, void *gx, flo
                    int64_t T, int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
     auto k = k3_bwd_kernel<VEC, FMHC_K3B_U, FMHC_K3B_MINB>;
-    k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
-        (const bf16 *)go, (const bf16 *)x, (const float4 *)hp, (bf16 *)gx, gh, T, C);
+    launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
+           (const bf16 *)x, (const float4 *)hp, (bf16 *)gx, gh, T, C);
   });
 }
 
@@ -426,9 +431,8 @@ void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *h
                    int64_t T, int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
     auto k = k4_fwd_kernel<VEC, FMHC_K4F_U, FMHC_K4F_MINB>;
-    k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
-        (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)out,
-        T, C);
+    launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)x,
+           (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)out, T, C);
   });
 }
 
@@ -436,9 +440,8 @@ void launch_grad_x_combine(const void *gx1, const void *gli, const float *hp, co
                            void *gx, int64_t T, int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
     auto k = grad_x_combine_kernel<VEC, 2>;
-    k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
-        (const bf16 *)gx1, (const bf16 *)gli, (const float4 *)hp, (const bf16 *)gx4, (bf16 *)gx,
-        T, C);
+    launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
+           (const bf16 *)gli, (const float4 *)hp, (const bf16 *)gx4, (bf16 *)gx, T, C);
   });
 }
 
@@ -447,9 +450,9 @@ void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H
                    int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
     auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB>;
-    k<<<grid_for(k, T, kThreads), kThreads, 0, s>>>(
-        (const bf16 *)go, (const bf16 *)x, (const bf16 *)lo, (const float4 *)H,
-        (const float4 *)hp, (bf16 *)gx, (bf16 *)glo, gH, ghp, T, C);
+    launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
+           (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)gx,
+           (bf16 *)glo, gH, ghp, T, C);
   });
 }
 
