@@ -47,6 +47,9 @@ namespace k1tc {
 #ifndef FMHC_K1B_ACC_BUFS   // grad_x TMEM accumulators (1 or 2)
 #define FMHC_K1B_ACC_BUFS 2
 #endif
+#ifndef FMHC_K1B_STORES_IN_FLIGHT  // grad_x TMA stores outstanding per CTA (1 or 2)
+#define FMHC_K1B_STORES_IN_FLIGHT 2
+#endif
 #ifndef FMHC_K1B_W_BUFS     // W chunk buffers (1 or 2)
 #define FMHC_K1B_W_BUFS 2
 #endif
@@ -372,6 +375,8 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     if (lane == 0) {
       int stage = 0;
       uint32_t phase = 0;
+      int prev = -1;
+      (void)prev;
       for (int64_t u = u0; u < u1 && !*abort; ++u) {
         int kc, tt;
         bwd_unit(u, a.ntt, kc, tt);
@@ -380,13 +385,24 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         tma_store_2d(&tmap_gx, base, kc * kBwdBK, tt * kBwdBT);
         tma_store_2d(&tmap_gx, base + kBwdXBox, kc * kBwdBK + 64, tt * kBwdBT);
         tma_store_commit();
+#if FMHC_K1B_STORES_IN_FLIGHT == 2
+        // Free the previous unit's stage once its store has read it, keeping
+        // this unit's store in flight.
+        tma_store_wait_read<1>();
+        if (prev >= 0) mbar_arrive(smem_u32(&sm.empty[prev]));
+        prev = stage;
+#else
         // Free the stage once this store has read it (the global writes may
         // still be in flight).
         tma_store_wait_read<0>();
         mbar_arrive(smem_u32(&sm.empty[stage]));
+#endif
         if (++stage == kBwdStages) { stage = 0; phase ^= 1; }
       }
       tma_store_wait_all<0>();
+#if FMHC_K1B_STORES_IN_FLIGHT == 2
+      if (prev >= 0) mbar_arrive(smem_u32(&sm.empty[prev]));
+#endif
     }
   }
 
