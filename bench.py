@@ -305,7 +305,7 @@ def run_ours(args):
         ms = float(tt.item())
 
     # --- end-to-end from host buffers --------------------------------------
-    e2e = run_e2e(args, hp, one_step, torch, dist, world, dev)
+    e2e = None if args.no_e2e else run_e2e(args, hp, one_step, torch, dist, world, dev)
     del hp
     torch.cuda.empty_cache()
 
@@ -326,7 +326,10 @@ def run_ours(args):
                           "frac": round(gbs / peaks["hbm_gbs"], 4)}
         dom = "k4_bwd"
         ach = bm[dom] / (kern_ms[dom] * 1e-3) / 1e9
-        tr = traffic.get(dom, {}).get("bytes_per_launch_full") if traffic else None
+        # ncu traffic applies only to the (T, C) it was scaled to
+        cap = traffic.get(dom, {}) if traffic else {}
+        tr = (cap.get("bytes_per_launch_full")
+              if cap.get("full_T") == T and cap.get("C", C) == C else None)
         sum_bytes = sum(bm.values())
         line = {
             "metric": METRIC, "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT,
@@ -338,7 +341,8 @@ def run_ours(args):
                        "T_per_gpu": T, "C": C, "n": N_STREAMS, "D": D_OUT,
                        "step": "K1f,K3f,K4f,K4b,K3b,K1b(dx+dW)" + (",allreduce(gW)" if world > 1 else ""),
                        "parallelism": f"token-sharded dp{world}",
-                       "l2": "inputs larger than L2 (x alone 512 MiB), no flush",
+                       "l2": f"inputs larger than L2 (x alone {T * N_STREAMS * C * 2 / 2**20:.0f} MiB), "
+                             "no flush",
                        "timing": "value: steps timed with events at the region's ends only; "
                                  "kernels/roofline: a second region of the same steps with an "
                                  "event pair around every op"},
@@ -782,6 +786,8 @@ def main():
     ap.add_argument("--block-T", type=int, default=65536, help="tokens per GPU for the block")
     ap.add_argument("--block-C", type=int, default=2048)
     ap.add_argument("--no-graphs", action="store_true", help="skip the small-batch graph measurement")
+    ap.add_argument("--no-e2e", action="store_true",
+                    help="skip the host-buffer e2e leg (its pinned buffers grow with --T/--C)")
     ap.add_argument("--small-T", type=int, default=8192)
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":

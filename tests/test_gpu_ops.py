@@ -333,3 +333,46 @@ def test_block_backward_pieces(T, C):
         if extra is not None:
             ref = ref + extra.float()
         torch.testing.assert_close(out.float(), ref, atol=BF_ATOL, rtol=BF_RTOL)
+
+
+def test_large_token_sharded_config_rows():
+    """The large per-GPU config (131,072 tokens x C = 4096: every (T, 4, C)
+    tensor has more than 2^31 elements).  All six ops run on the full tensors;
+    a sample of rows, first and last included, is checked against a float32
+    restatement, so 64-bit offsets and the last partial tiles are exercised."""
+    T, C = 131072, 4096
+    ops = torch.ops.flash_mhc
+    g = torch.Generator(device="cuda").manual_seed(11)
+    rn = lambda *s, std=1.0: (torch.randn(*s, device="cuda", generator=g) * std)  # noqa: E731
+    x = rn(T, 4, C).bfloat16()
+    W = rn(32, 4 * C, std=0.02).bfloat16()
+    lo = rn(T, C).bfloat16()
+    hp, hq, H = rn(T, 4), rn(T, 4), rn(T, 4, 4)
+    gp, g3, g4 = rn(T, 32).bfloat16(), rn(T, C).bfloat16(), rn(T, 4, C).bfloat16()
+    xf = x.view(T, 4 * C)
+    proj, inv = ops.fused_rmsnorm_project(xf, W)
+    li = ops.fused_pre_map(x, hp)
+    out = ops.fused_post_res(x, lo, H, hq)
+    gx4, glo, gH, ghp = ops.fused_post_res_backward(g4, x, lo, H, hq)
+    gx3, gh3 = ops.fused_pre_map_backward(g3, x, hp)
+    gx1, gW = ops.fused_rmsnorm_project_backward(gp, xf, W, proj, inv)
+    rows = torch.cat([torch.arange(0, 64), torch.randint(64, T - 64, (192,), generator=torch.Generator().manual_seed(5)),
+                      torch.arange(T - 64, T)]).cuda()
+    f = lambda t: t[rows].float()  # noqa: E731
+    xr, xfr, lor, g4r, g3r = f(x), f(xf), f(lo), f(g4), f(g3)
+    rinv = torch.rsqrt((xfr ** 2).mean(1) + 1e-6)
+    torch.testing.assert_close(inv[rows], rinv, atol=0, rtol=1e-5)
+    torch.testing.assert_close(f(proj), (xfr @ W.float().t()) * rinv[:, None], atol=BF_ATOL, rtol=BF_RTOL)
+    torch.testing.assert_close(f(li), (hp[rows][:, :, None] * xr).sum(1), atol=BF_ATOL, rtol=BF_RTOL)
+    Hr, hqr = H[rows], hq[rows]
+    torch.testing.assert_close(f(out), torch.einsum("tij,tjc->tic", Hr, xr) + hqr[:, :, None] * lor[:, None, :],
+                               atol=BF_ATOL, rtol=BF_RTOL)
+    torch.testing.assert_close(f(gx4), torch.einsum("tij,tic->tjc", Hr, g4r), atol=BF_ATOL, rtol=BF_RTOL)
+    torch.testing.assert_close(f(glo), (hqr[:, :, None] * g4r).sum(1), atol=BF_ATOL, rtol=BF_RTOL)
+    torch.testing.assert_close(gH[rows], torch.einsum("tic,tjc->tij", g4r, xr), atol=1e-1, rtol=1e-3)
+    torch.testing.assert_close(gx3[rows].float(), hp[rows][:, :, None] * g3r[:, None, :], atol=BF_ATOL, rtol=BF_RTOL)
+    torch.testing.assert_close(gh3[rows], (xr * g3r[:, None, :]).sum(2), atol=1e-1, rtol=1e-3)
+    s = (f(gp) * f(proj)).sum(1) * inv[rows] ** 2 / (4 * C)
+    rgx1 = inv[rows][:, None] * (f(gp) @ W.float()) - s[:, None] * xfr
+    torch.testing.assert_close(f(gx1), rgx1, atol=BF_ATOL, rtol=BF_RTOL)
+    assert torch.isfinite(gW.float()).all()
