@@ -114,7 +114,7 @@ def _run(blk, x, g, fused):
     return out.detach(), xx.grad, {n: p.grad.clone() for n, p in blk.named_parameters()}
 
 
-@pytest.mark.parametrize("T,C", [(4096, 1024), (65537, 768)])
+@pytest.mark.parametrize("T,C", [(4096, 1024), (65537, 768), (65536, 2048)])  # last: the block config
 def test_fused_vs_pytorch_path_same_gpu(T, C):
     blk = _make(T, C, 1).train()
     torch.manual_seed(2)
