@@ -373,8 +373,7 @@ bool device_is_sm100() {
 
 const char *k1_tc_error() { return k1tc::g_msg; }
 
-static_assert((sizeof(k1tc::BwdSmem) + 1024) * FMHC_K1B_CTAS_PER_SM <= 232448,
-              "K1 backward shared memory");
+static_assert(sizeof(k1tc::BwdSmem) + 1024 <= 232448, "K1 backward shared memory");
 static_assert((sizeof(k1tc::FwdSmem) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
               "K1 forward shared memory");
 
@@ -413,32 +412,44 @@ namespace k1tc {
 namespace {
 
 struct BwdPlan {
-  int ntt, nkc, grid, maxseg;
-  int64_t units;
+  int ntt, nkc, G, ngroups, grid, base, rem;
   int64_t gos_bytes, sinv_bytes, part_bytes;
 };
 
 int64_t round256(int64_t b) { return (b + 255) & ~int64_t(255); }
 
+// Work split of the backward kernel (see k1_tc_bwd.cuh): the nkc k-chunks form
+// nkc / G groups, the grid's CTAs are spread over the groups as evenly as
+// possible (the first `rem` groups get base + 1 CTAs, the rest base), and CTA
+// i of a group of ng takes the token tiles i, i + ng, ...  G (a divisor of
+// nkc, at most 8) is chosen to minimise the largest per-CTA unit count, the
+// larger G on ties.
 BwdPlan bwd_plan(int64_t T, int64_t nC) {
   BwdPlan p{};
   p.ntt = int((T + kBwdBT - 1) / kBwdBT);
   p.nkc = int(nC / kBwdBK);
-  p.units = int64_t(p.nkc) * p.ntt;
-  int64_t g = int64_t(device_sms()) * FMHC_K1B_CTAS_PER_SM;
-  if (g > p.units) g = p.units;
-  if (g < 1) g = 1;
-  p.grid = int(g);
-  p.maxseg = 1;
-  for (int c = 0; c < p.grid; ++c) {
-    const int64_t c0 = int64_t(c) * p.units / p.grid, c1 = int64_t(c + 1) * p.units / p.grid;
-    if (c1 <= c0) continue;
-    const int segs = int((c1 - 1) / p.ntt - c0 / p.ntt + 1);
-    if (segs > p.maxseg) p.maxseg = segs;
+  const int sms = device_sms();
+  int64_t best_cost = -1;
+  for (int G = kBwdMaxG; G >= 1; G >>= 1) {
+    if (p.nkc % G) continue;
+    const int ngroups = p.nkc / G;
+    int64_t grid = int64_t(ngroups) * p.ntt;
+    if (grid > sms) grid = sms;
+    if (grid < ngroups) continue;  // every group needs a CTA
+    const int base = int(grid / ngroups);
+    const int64_t cost = int64_t(G) * ((p.ntt + base - 1) / base);
+    if (best_cost < 0 || cost < best_cost) {
+      best_cost = cost;
+      p.G = G;
+      p.ngroups = ngroups;
+      p.grid = int(grid);
+      p.base = base;
+      p.rem = int(grid % ngroups);
+    }
   }
   p.gos_bytes = round256(T * kND * 2);
   p.sinv_bytes = round256(int64_t(p.ntt) * kBwdBT * 8);
-  p.part_bytes = round256(int64_t(p.grid) * p.maxseg * kND * kBwdBK * 4);
+  p.part_bytes = round256(int64_t(p.grid) * p.G * kND * kBwdBK * 4);
   return p;
 }
 
@@ -448,6 +459,8 @@ BwdPlan bwd_plan(int64_t T, int64_t nC) {
 bool k1_tc_bwd_supported(const void *go, const void *x, const void *W, const void *proj,
                          const void *gx, int64_t T, int64_t nC, int64_t D) {
   if (D != k1tc::kND || nC % k1tc::kBwdBK != 0 || T < 1 || T > (int64_t(1) << 31)) return false;
+  // Each group of at most 8 k-chunks needs its own CTA.
+  if (nC / k1tc::kBwdBK > int64_t(k1tc::kBwdMaxG) * k1tc::device_sms()) return false;
   const uintptr_t m = reinterpret_cast<uintptr_t>(go) | reinterpret_cast<uintptr_t>(x) |
                       reinterpret_cast<uintptr_t>(W) | reinterpret_cast<uintptr_t>(proj) |
                       reinterpret_cast<uintptr_t>(gx);
@@ -456,7 +469,8 @@ bool k1_tc_bwd_supported(const void *go, const void *x, const void *W, const voi
 }
 
 int64_t k1_tc_bwd_workspace_bytes(int64_t T, int64_t nC) {
-  if (T < 1 || nC % k1tc::kBwdBK) return 0;
+  if (T < 1 || nC < k1tc::kBwdBK || nC % k1tc::kBwdBK) return 0;
+  if (nC / k1tc::kBwdBK > int64_t(k1tc::kBwdMaxG) * k1tc::device_sms()) return 0;
   const k1tc::BwdPlan p = k1tc::bwd_plan(T, nC);
   return p.gos_bytes + p.sinv_bytes + p.part_bytes;
 }
@@ -513,14 +527,15 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.T = T;
   args.nC = nC;
   args.ntt = p.ntt;
-  args.units = p.units;
-  args.maxseg = p.maxseg;
+  args.G = p.G;
+  args.base = p.base;
+  args.rem = p.rem;
   args.with_dw = with_dw ? 1 : 0;
   launch(k1_bwd_tc_kernel, dim3(unsigned(p.grid)), dim3(kBwdThreads), smem, s, mx, mgx, mgo, mgos,
          mw, args);
   if (with_dw) {
     launch(k1_bwd_dw_reduce_kernel, dim3(unsigned(p.nkc), kND), dim3(kBwdBK), 0, s, part,
-           static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.units, p.grid, p.maxseg);
+           static_cast<__nv_bfloat16 *>(gW), nC, p.ntt, p.G, p.base, p.rem);
   }
   return 0;
 }
