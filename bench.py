@@ -229,7 +229,8 @@ class HotPath:
                                                                  outs["proj"], outs["inv_rms"]))
         return outs
 
-    LAUNCHES_PER_STEP = 8
+    # K1f, K3f, K4f, K4b, K3b, K1b main kernel + its grad_W reduce
+    LAUNCHES_PER_STEP = 7
 
 
 def _allreduce_gw(torch, dist, outs):

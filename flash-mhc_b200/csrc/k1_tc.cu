@@ -413,7 +413,7 @@ namespace {
 
 struct BwdPlan {
   int ntt, nkc, G, ngroups, grid, base, rem;
-  int64_t gos_bytes, sinv_bytes, part_bytes;
+  int64_t part_bytes;
 };
 
 int64_t round256(int64_t b) { return (b + 255) & ~int64_t(255); }
@@ -447,8 +447,6 @@ BwdPlan bwd_plan(int64_t T, int64_t nC) {
       p.rem = int(grid % ngroups);
     }
   }
-  p.gos_bytes = round256(T * kND * 2);
-  p.sinv_bytes = round256(int64_t(p.ntt) * kBwdBT * 8);
   p.part_bytes = round256(int64_t(p.grid) * p.G * kND * kBwdBK * 4);
   return p;
 }
@@ -472,7 +470,7 @@ int64_t k1_tc_bwd_workspace_bytes(int64_t T, int64_t nC) {
   if (T < 1 || nC < k1tc::kBwdBK || nC % k1tc::kBwdBK) return 0;
   if (nC / k1tc::kBwdBK > int64_t(k1tc::kBwdMaxG) * k1tc::device_sms()) return 0;
   const k1tc::BwdPlan p = k1tc::bwd_plan(T, nC);
-  return p.gos_bytes + p.sinv_bytes + p.part_bytes;
+  return p.part_bytes;
 }
 
 int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *proj,
@@ -481,27 +479,22 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   using namespace k1tc;
   const BwdPlan p = bwd_plan(T, nC);
   const bool with_dw = gW != nullptr;
-  uint8_t *gos = nullptr;
-  float2 *sinv = nullptr;
   float *part = nullptr;
   if (with_dw) {
-    const int64_t need = p.gos_bytes + p.sinv_bytes + p.part_bytes;
-    if (ws == nullptr || ws_bytes < need || (reinterpret_cast<uintptr_t>(ws) & 255)) {
+    if (ws == nullptr || ws_bytes < p.part_bytes || (reinterpret_cast<uintptr_t>(ws) & 255)) {
       snprintf(g_msg, sizeof(g_msg), "workspace of %lld bytes (need %lld, 256-byte aligned)",
-               (long long)ws_bytes, (long long)need);
+               (long long)ws_bytes, (long long)p.part_bytes);
       return 6;
     }
-    gos = static_cast<uint8_t *>(ws);
-    sinv = reinterpret_cast<float2 *>(gos + p.gos_bytes);
-    part = reinterpret_cast<float *>(gos + p.gos_bytes + p.sinv_bytes);
+    part = static_cast<float *>(ws);
   }
-  CUtensorMap mx, mgx, mgo, mgos, mw;
+  CUtensorMap mx, mgx, mgo, mproj, mw;
   bool ok = make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBwdBT,
                      CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map(&mgx, gx, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBwdBT,
                      CU_TENSOR_MAP_SWIZZLE_128B) &&
             make_map(&mgo, go, kND, uint64_t(T), kND * 2, kND, kBwdBT, CU_TENSOR_MAP_SWIZZLE_64B) &&
-            make_map(&mgos, with_dw ? gos : go, kND, uint64_t(T), kND * 2, kND, kBwdBT,
+            make_map(&mproj, proj, kND, uint64_t(T), kND * 2, kND, kBwdBT,
                      CU_TENSOR_MAP_SWIZZLE_64B) &&
             make_map(&mw, W, uint64_t(nC), kND, uint64_t(nC) * 2, 64, kND,
                      CU_TENSOR_MAP_SWIZZLE_128B);
@@ -509,20 +502,10 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
     snprintf(g_msg, sizeof(g_msg), "cuTensorMapEncodeTiled failed");
     return 5;
   }
-  if (with_dw) {
-    const int64_t T_pad = int64_t(p.ntt) * kBwdBT;
-    // 4 threads per token
-    launch(k1_bwd_prep_kernel, dim3(unsigned(T_pad / 64)), dim3(256), 0, s,
-           static_cast<const __nv_bfloat16 *>(go), static_cast<const __nv_bfloat16 *>(proj),
-           inv_rms, reinterpret_cast<__nv_bfloat16 *>(gos), sinv, T, T_pad, nC);
-  }
   const size_t smem = sizeof(BwdSmem) + 1024;
   if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_bwd_tc_kernel), smem)) return e;
   BwdArgs args;
-  args.go = static_cast<const __nv_bfloat16 *>(go);
-  args.proj = static_cast<const __nv_bfloat16 *>(proj);
   args.inv_rms = inv_rms;
-  args.sinv = sinv;
   args.dw_part = part;
   args.T = T;
   args.nC = nC;
@@ -531,7 +514,7 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
   args.base = p.base;
   args.rem = p.rem;
   args.with_dw = with_dw ? 1 : 0;
-  launch(k1_bwd_tc_kernel, dim3(unsigned(p.grid)), dim3(kBwdThreads), smem, s, mx, mgx, mgo, mgos,
+  launch(k1_bwd_tc_kernel, dim3(unsigned(p.grid)), dim3(kBwdThreads), smem, s, mx, mgx, mgo, mproj,
          mw, args);
   if (with_dw) {
     launch(k1_bwd_dw_reduce_kernel, dim3(unsigned(p.nkc), kND), dim3(kBwdBK), 0, s, part,

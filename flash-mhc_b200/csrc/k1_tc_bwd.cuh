@@ -18,11 +18,10 @@
 // G x 256 contiguous bytes per tile, and each CTA accumulates the grad_W
 // partials of its G k-chunks in TMEM over all its tiles.
 //
-//   warp 0     TMA producer: per token tile go[128 t x 32] and gos[128 t x 32]
-//              (64-byte swizzle) and the tile's (s, inv_rms) pairs into a tile
-//              slot (two slots); per unit x[128 t x 128 k] (two 64-column
-//              boxes, 128-byte swizzle) and the W chunk [32 x 128 k] into a
-//              stage (four stages).
+//   warp 0     TMA producer: per token tile go[128 t x 32] and proj[128 t x 32]
+//              (64-byte swizzle) into a tile slot (two slots); per unit
+//              x[128 t x 128 k] (two 64-column boxes, 128-byte swizzle) and the
+//              W chunk [32 x 128 k] into a stage (four stages).
 //   warp 1     MMA issuer, per unit:
 //                grad_W: D2_j[k, d] += x^T (MN-major A) * gos (MN-major B),
 //                        8 x M128 N32 K16 into accumulator j of the group;
@@ -36,10 +35,12 @@
 //   warp 10    store: TMA-stores each unit's grad_x from its stage, keeps up to
 //              two stores in flight and frees a stage as soon as its store has
 //              read it.
-// A prep kernel computes per token s and inv_rms (float2) and the grad_W
-// operand gos.  A final small kernel reduces the per-CTA grad_W partials of
-// each group in a fixed order (deterministic) and rounds to bf16.  Without a
-// workspace (grad_x only) the epilogue computes s itself from go and proj.
+//   warp 11    tile prep, once per token tile: (s, inv_rms) per token and the
+//              grad_W operand gos = bf16(go * inv_rms) (same 64-byte swizzle
+//              as go) into the slot, from the slot's go and proj and inv_rms.
+// A final small kernel reduces the per-CTA grad_W partials of each group in a
+// fixed order (deterministic) and rounds to bf16.  The grad_x-only variant
+// runs the same kernel without the grad_W MMAs and needs no workspace.
 #pragma once
 
 namespace fmhc {
@@ -59,25 +60,29 @@ constexpr int kBwdStages = FMHC_K1B_STAGES;
 constexpr int kBwdInflight = FMHC_K1B_STORES_IN_FLIGHT;
 static_assert(kBwdInflight >= 1 && kBwdInflight <= 3 && kBwdInflight < kBwdStages,
               "stores in flight");
-constexpr int kBwdSlots = 2;                      // token-tile slots (go, gos, (s, inv))
+constexpr int kBwdSlots = 2;                      // token-tile slots (go, proj, gos, (s, inv))
 constexpr int kBwdMaxG = 8;                       // k-chunks per group (TMEM: 8 x 32 columns)
 constexpr int kBwdXBytes = kBwdBT * kBwdBK * 2;   // 32 KiB (two 16 KiB boxes)
 constexpr int kBwdXBox = kBwdBT * 64 * 2;         // 16 KiB
 constexpr int kBwdWBytes = kND * kBwdBK * 2;      // 8 KiB  (two 4 KiB boxes)
 constexpr int kBwdStageBytes = kBwdXBytes + kBwdWBytes;  // 40 KiB
-constexpr int kBwdGBytes = kBwdBT * kND * 2;      // 8 KiB  (go or gos tile)
+constexpr int kBwdGBytes = kBwdBT * kND * 2;      // 8 KiB  (go, proj or gos tile)
 constexpr int kBwdSBytes = kBwdBT * 8;            // 1 KiB  ((s, inv_rms) per token)
-constexpr int kBwdSlotBytes = 2 * kBwdGBytes + kBwdSBytes;  // 17 KiB
-constexpr int kBwdThreads = 352;                  // producer, MMA, 8 epilogue warps, store
+// Slot layout: go at 0, proj at 8 KiB (TMA), gos at 16 KiB, (s, inv) at 24 KiB (prep warp).
+constexpr int kBwdSlotGo = 0, kBwdSlotProj = kBwdGBytes, kBwdSlotGos = 2 * kBwdGBytes,
+              kBwdSlotSinv = 3 * kBwdGBytes;
+constexpr int kBwdSlotBytes = 3 * kBwdGBytes + kBwdSBytes;  // 25 KiB
+constexpr int kBwdThreads = 384;                  // producer, MMA, 8 epilogue warps, store, prep
 constexpr int kBwdEpiWarps = 8;
 constexpr int kBwdStoreWarp = 2 + kBwdEpiWarps;
+constexpr int kBwdPrepWarp = kBwdStoreWarp + 1;
 // Two 128-column grad_x accumulators, then up to 8 x 32 grad_W columns.
 constexpr uint32_t kBwdTmemCols = 512;
 constexpr uint32_t kBwdDwCol = 256;
 
 struct alignas(1024) BwdSmem {
   uint8_t stage[kBwdStages][kBwdStageBytes];  // x tile, then the W chunk
-  uint8_t slot[kBwdSlots][kBwdSlotBytes];     // go, gos, (s, inv) of one token tile
+  uint8_t slot[kBwdSlots][kBwdSlotBytes];     // go, proj, gos, (s, inv) of one token tile
   uint64_t full[kBwdStages];
   uint64_t empty[kBwdStages];
   // epi[s]: the 8 epilogue warps finished writing grad_x into stage s.  Its
@@ -85,7 +90,8 @@ struct alignas(1024) BwdSmem {
   // before the store warp has waited on this phase and freed the stage, so
   // phases never alias and each counts one unit's arrivals.
   uint64_t epi[kBwdStages];
-  uint64_t gfull[kBwdSlots];
+  uint64_t gfull[kBwdSlots];   // go and proj landed
+  uint64_t gready[kBwdSlots];  // prep warp wrote gos and (s, inv)
   uint64_t gempty[kBwdSlots];  // MMA commit after the tile's last unit + 8 epilogue warps
   uint64_t tfull[2];
   uint64_t tempty[2];
@@ -98,13 +104,10 @@ struct alignas(1024) BwdSmem {
 enum : unsigned { kSiteBProdEmpty = 0x201, kSiteBProdSlot = 0x202, kSiteBMmaFull = 0x203,
                   kSiteBMmaTempty = 0x204, kSiteBMmaSlot = 0x205, kSiteBEpiSlot = 0x206,
                   kSiteBEpiFull = 0x207, kSiteBEpiTfull = 0x208, kSiteBEpiDw = 0x209,
-                  kSiteBDrain = 0x20a, kSiteBEpiStore = 0x20b };
+                  kSiteBDrain = 0x20a, kSiteBEpiStore = 0x20b, kSiteBPrepSlot = 0x20c };
 
 struct BwdArgs {
-  const __nv_bfloat16 *go;    // (T, 32)
-  const __nv_bfloat16 *proj;  // (T, 32)
   const float *inv_rms;       // (T,)
-  const float2 *sinv;         // (ntt*128,) (s, inv_rms) per token, or nullptr
   float *dw_part;             // [grid][G][32][128] f32 (only with_dw)
   int64_t T;
   int nC;
@@ -134,9 +137,7 @@ __host__ __device__ __forceinline__ int bwd_group_first_cta(int g, int base, int
 }
 
 // Partial dot product of one 16-byte chunk (8 of the 32 d) of go and proj.
-// The full dot product is (p0 + p1) + (p2 + p3) over the four chunks, in this
-// order in both places that compute it (prep kernel, no-workspace epilogue),
-// so grad_x is identical whichever entry point computed it.
+// The full dot product is (p0 + p1) + (p2 + p3) over the four chunks.
 __device__ __forceinline__ float go_proj_chunk_dot(const uint4 g, const uint4 p) {
   float dot = 0.f;
   dot = fmaf(bf16lo(g.x), bf16lo(p.x), dot); dot = fmaf(bf16hi(g.x), bf16hi(p.x), dot);
@@ -150,7 +151,7 @@ __global__ void __launch_bounds__(kBwdThreads, 1)
 k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_gx,
                  const __grid_constant__ CUtensorMap tmap_go,
-                 const __grid_constant__ CUtensorMap tmap_gos,
+                 const __grid_constant__ CUtensorMap tmap_proj,
                  const __grid_constant__ CUtensorMap tmap_w, const BwdArgs a) {
   extern __shared__ uint8_t smem_raw[];
   BwdSmem &sm = *reinterpret_cast<BwdSmem *>(
@@ -173,6 +174,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     }
     for (int b = 0; b < kBwdSlots; ++b) {
       mbar_init(smem_u32(&sm.gfull[b]), 1);
+      mbar_init(smem_u32(&sm.gready[b]), 1);
       mbar_init(smem_u32(&sm.gempty[b]), 1 + kBwdEpiWarps);
     }
     for (int b = 0; b < 2; ++b) {
@@ -186,7 +188,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     prefetch_tmap(&tmap_x);
     prefetch_tmap(&tmap_gx);
     prefetch_tmap(&tmap_go);
-    prefetch_tmap(&tmap_gos);
+    prefetch_tmap(&tmap_proj);
     prefetch_tmap(&tmap_w);
   }
   if (warp == 1) {
@@ -205,19 +207,18 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     if (lane == 0) {
       int stage = 0, slot = 0, issued = 0, slots_issued = 0;
       uint32_t phase = 0, sphase = 0;
-      const uint32_t gtx = uint32_t((a.with_dw ? 2 : 1) * kBwdGBytes + (a.sinv ? kBwdSBytes : 0));
+      const uint32_t gtx = uint32_t(2 * kBwdGBytes);
       for (int j = 0; j < nunits && !*abort; ++j) {
         const int m = j / G, jj = j - m * G;
         const int32_t row0 = (gi + m * ng) * kBwdBT;
         const int kc = grp * G + jj;
-        if (jj == 0) {  // new token tile: go, gos, (s, inv) into the next slot
+        if (jj == 0) {  // new token tile: go and proj into the next slot
           if (!mbar_wait(smem_u32(&sm.gempty[slot]), sphase ^ 1, abort, kSiteBProdSlot)) break;
           const uint32_t gf = smem_u32(&sm.gfull[slot]);
           const uint32_t sb = smem_u32(sm.slot[slot]);
           mbar_arrive_expect_tx(gf, gtx);
-          tma_load_2d(sb, &tmap_go, gf, 0, row0);
-          if (a.with_dw) tma_load_2d(sb + kBwdGBytes, &tmap_gos, gf, 0, row0);
-          if (a.sinv) bulk_load(sb + 2 * kBwdGBytes, a.sinv + row0, kBwdSBytes, gf);
+          tma_load_2d(sb + kBwdSlotGo, &tmap_go, gf, 0, row0);
+          tma_load_2d(sb + kBwdSlotProj, &tmap_proj, gf, 0, row0);
           ++slots_issued;
           if (++slot == kBwdSlots) { slot = 0; sphase ^= 1; }
         }
@@ -259,7 +260,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       for (int j = 0; j < nunits && !*abort; ++j) {
         const int m = j / G, jj = j - m * G;
         if (jj == 0 &&
-            !mbar_wait(smem_u32(&sm.gfull[slot]), sphase, abort, kSiteBMmaSlot)) { ok = false; break; }
+            !mbar_wait(smem_u32(&sm.gready[slot]), sphase, abort, kSiteBMmaSlot)) { ok = false; break; }
         if (!mbar_wait(smem_u32(&sm.tempty[acc]), acc_phase ^ 1, abort, kSiteBMmaTempty)) { ok = false; break; }
         if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteBMmaFull)) { ok = false; break; }
         tc_fence_after();
@@ -270,7 +271,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 #pragma unroll
           for (int k = 0; k < kBwdBT / 16; ++k) {
             const uint64_t ad = smem_desc(base + k * 2048, kBwdXBox, 1024, 2);
-            const uint64_t bd = smem_desc(gs + kBwdGBytes + k * 1024, 512, 512, 4);
+            const uint64_t bd = smem_desc(gs + kBwdSlotGos + k * 1024, 512, 512, 4);
             mma_bf16_ss(tmem + kBwdDwCol + uint32_t(jj * kND), ad, bd, idesc_dw,
                         (m > 0 || k > 0) ? 1u : 0u);
           }
@@ -280,7 +281,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           const uint32_t wb = base + kBwdXBytes;
 #pragma unroll
           for (int k = 0; k < kND / 16; ++k) {
-            const uint64_t ad = smem_desc(gs + k * 32, 16, 512, 4);
+            const uint64_t ad = smem_desc(gs + kBwdSlotGo + k * 32, 16, 512, 4);
             const uint64_t bd = smem_desc(wb + k * 2048, kBwdWBytes / 2, 1024, 2);
             mma_bf16_ss(tmem + uint32_t(acc * kBwdBK), ad, bd, idesc_dx, k != 0);
           }
@@ -310,27 +311,10 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       const int m = j / G, jj = j - m * G;
       if (jj == 0) {
         // (s, inv_rms) of this thread's token, kept in registers for the tile.
-        const int64_t t = int64_t(gi + m * ng) * kBwdBT + r;
-        if (!mbar_wait(smem_u32(&sm.gfull[slot]), sphase, abort, kSiteBEpiSlot)) { ok = false; break; }
-        if (a.sinv) {
-          const float2 si = reinterpret_cast<const float2 *>(sm.slot[slot] + 2 * kBwdGBytes)[r];
-          s = si.x;
-          inv = si.y;
-        } else {
-          // No workspace: s = (go . proj) * inv^2 / nC from the stored forward output.
-          s = 0.f;
-          inv = 0.f;
-          if (t < a.T) {
-            inv = a.inv_rms[t];
-            const uint4 *g4 = reinterpret_cast<const uint4 *>(a.go + t * kND);
-            const uint4 *p4 = reinterpret_cast<const uint4 *>(a.proj + t * kND);
-            float pc[4];
-#pragma unroll
-            for (int c = 0; c < 4; ++c) pc[c] = go_proj_chunk_dot(__ldg(g4 + c), __ldg(p4 + c));
-            const float dot = (pc[0] + pc[1]) + (pc[2] + pc[3]);
-            s = dot * (inv * inv) / float(a.nC);
-          }
-        }
+        if (!mbar_wait(smem_u32(&sm.gready[slot]), sphase, abort, kSiteBEpiSlot)) { ok = false; break; }
+        const float2 si = reinterpret_cast<const float2 *>(sm.slot[slot] + kBwdSlotSinv)[r];
+        s = si.x;
+        inv = si.y;
         // The slot's refill is a TMA (async-proxy) write: order this thread's
         // generic-proxy read before it, then release (one arrive per warp).
         fence_proxy_async_smem();
@@ -390,7 +374,7 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         for (int d = 0; d < kND; ++d) __stcg(dst + d * kBwdBK, __uint_as_float(v[d]));
       }
     }
-  } else {
+  } else if (warp == kBwdStoreWarp) {
     // --------------------------------------------------------------- store
     if (lane == 0) {
       int stage = 0, npend = 0;
@@ -419,6 +403,53 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       tma_store_wait_all<0>();
       for (int i = 0; i < npend; ++i) mbar_arrive(smem_u32(&sm.empty[pend[i]]));
     }
+  } else if (warp == kBwdPrepWarp) {
+    // ----------------------------------------------------------- tile prep
+    // Lane l takes the tile rows l, l + 32, l + 64, l + 96.  Rows of go, proj
+    // and gos are 64 bytes with the TMA's 64-byte swizzle: 16-byte chunk c of
+    // row r sits at chunk position c ^ ((r >> 1) & 3).
+    int slot = 0;
+    uint32_t sphase = 0;
+    for (int m = 0; m < ntiles && !*abort; ++m) {
+      const int64_t t0 = int64_t(gi + m * ng) * kBwdBT;
+      float invr[4];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int64_t t = t0 + lane + 32 * i;
+        invr[i] = t < a.T ? __ldg(a.inv_rms + t) : 0.f;
+      }
+      if (!mbar_wait(smem_u32(&sm.gfull[slot]), sphase, abort, kSiteBPrepSlot)) break;
+      uint8_t *sb = sm.slot[slot];
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const int r = lane + 32 * i;
+        const float rinv = invr[i];
+        float pc[4];
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          const int off = r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+          const uint4 g = *reinterpret_cast<const uint4 *>(sb + kBwdSlotGo + off);
+          const uint4 pj = *reinterpret_cast<const uint4 *>(sb + kBwdSlotProj + off);
+          pc[c] = go_proj_chunk_dot(g, pj);
+          // gos = bf16(go * inv_rms), as the reference's (grad_out * inv_rms).to(x.dtype)
+          uint4 o;
+          o.x = pack_bf16x2(bf16lo(g.x) * rinv, bf16hi(g.x) * rinv);
+          o.y = pack_bf16x2(bf16lo(g.y) * rinv, bf16hi(g.y) * rinv);
+          o.z = pack_bf16x2(bf16lo(g.z) * rinv, bf16hi(g.z) * rinv);
+          o.w = pack_bf16x2(bf16lo(g.w) * rinv, bf16hi(g.w) * rinv);
+          *reinterpret_cast<uint4 *>(sb + kBwdSlotGos + off) = o;
+        }
+        const float dot = (pc[0] + pc[1]) + (pc[2] + pc[3]);
+        reinterpret_cast<float2 *>(sb + kBwdSlotSinv)[r] =
+            make_float2(dot * (rinv * rinv) / float(a.nC), rinv);
+      }
+      // gos is read by the MMA (async proxy) and go/proj are refilled by the
+      // TMA: order this thread's generic reads and writes before both.
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(smem_u32(&sm.gready[slot]));
+      if (++slot == kBwdSlots) { slot = 0; sphase ^= 1; }
+    }
   }
 
   tc_fence_before();
@@ -427,44 +458,6 @@ k1_bwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     tc_fence_after();
     tmem_dealloc(tmem, kBwdTmemCols);
   }
-}
-
-// Per token: sinv[t] = (s, inv_rms) with s = (go . proj) * inv_rms^2 / nC,
-// and (when gos != nullptr) gos[t, :] = bf16(go[t, :] * inv_rms[t]), the
-// grad_W operand, rounded like the reference's (grad_out * inv_rms).to(x.dtype).
-// Four threads per token, one 16-byte chunk of go and proj each; the chunk
-// dot products are combined with two shuffles.  Rows T .. T_pad-1 of sinv
-// are zeroed.  The grid covers exactly 4 * T_pad threads (T_pad is a multiple
-// of 128), so every warp is whole.
-__global__ void __launch_bounds__(256)
-k1_bwd_prep_kernel(const __nv_bfloat16 *__restrict__ go, const __nv_bfloat16 *__restrict__ proj,
-                   const float *__restrict__ inv_rms, __nv_bfloat16 *__restrict__ gos,
-                   float2 *__restrict__ sinv, int64_t T, int64_t T_pad, int nC) {
-  pdl_wait();
-  const int64_t i = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  const int64_t t = i >> 2;
-  const int c = int(i & 3);
-  if (t >= T_pad) return;  // never splits a warp (see above)
-  const bool valid = t < T;
-  float r = 0.f, dot = 0.f;
-  uint4 g = make_uint4(0, 0, 0, 0);
-  if (valid) {
-    r = inv_rms[t];
-    g = __ldg(reinterpret_cast<const uint4 *>(go + t * kND) + c);
-    const uint4 p = __ldg(reinterpret_cast<const uint4 *>(proj + t * kND) + c);
-    dot = go_proj_chunk_dot(g, p);
-  }
-  dot += __shfl_xor_sync(0xffffffffu, dot, 1);
-  dot += __shfl_xor_sync(0xffffffffu, dot, 2);
-  if (valid && gos) {
-    uint4 o;
-    o.x = pack_bf16x2(bf16lo(g.x) * r, bf16hi(g.x) * r);
-    o.y = pack_bf16x2(bf16lo(g.y) * r, bf16hi(g.y) * r);
-    o.z = pack_bf16x2(bf16lo(g.z) * r, bf16hi(g.z) * r);
-    o.w = pack_bf16x2(bf16lo(g.w) * r, bf16hi(g.w) * r);
-    reinterpret_cast<uint4 *>(gos + t * kND)[c] = o;
-  }
-  if (c == 0) sinv[t] = valid ? make_float2(dot * (r * r) / float(nC), r) : make_float2(0.f, 0.f);
 }
 
 // grad_W[d, k] = bf16(sum of the grad_W partials of the CTAs of k's group),

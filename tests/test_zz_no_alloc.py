@@ -94,8 +94,16 @@ def test_no_alloc_matches_workspace_entry_point(T, nC):
 
 def test_no_alloc_rejects_sizes_above_its_scratch():
     L = _lib()
+    L.fmhc_k1_bwd_workspace_size.argtypes = [_i64, _i64, _i64]
+    L.fmhc_k1_bwd_workspace_size.restype = _i64
+    # nC = 16400 is not a multiple of 128, so this shape takes the CUDA-core
+    # path, whose workspace (16 x 32 x nC f32) is above the 32 MiB scratch.
+    # The size is checked first: the call below hands the entry point a
+    # 32-byte dummy buffer and must be rejected before any launch.
+    T, nC = 1 << 22, 16400
+    assert L.fmhc_k1_bwd_workspace_size(T, nC, 32) > (32 << 20)
     dummy = torch.empty(16, device="cuda", dtype=torch.bfloat16)
     p = dummy.data_ptr()
-    st = L.fmhc_k1_bwd_noalloc(p, p, p, p, p, p, p, 1 << 22, 16384, 32, None)
+    st = L.fmhc_k1_bwd_noalloc(p, p, p, p, p, p, p, T, nC, 32, None)
     assert st == 6  # FMHC_ERR_WORKSPACE, before any launch
     assert "maximum" in L.fmhc_last_error().decode()
