@@ -422,14 +422,19 @@ int64_t round256(int64_t b) { return (b + 255) & ~int64_t(255); }
 // nkc / G groups, the grid's CTAs are spread over the groups as evenly as
 // possible (the first `rem` groups get base + 1 CTAs, the rest base), and CTA
 // i of a group of ng takes the token tiles i, i + ng, ...  G (a divisor of
-// nkc, at most 8) is chosen to minimise the largest per-CTA unit count, the
-// larger G on ties.
+// nkc, at most 8) minimises an estimate of the kernel time fitted to
+// measurements at nC = 4096 (T = 8192 and 65536, G = 2, 4, 8):
+//   1.56 us per unit of the busiest CTA (64 KiB of HBM traffic)
+// + 0.28 us per token tile of the busiest CTA (slot load and tile prep)
+// + the grad_W partials, G x 16 KiB per CTA written and read back, at 6 TB/s.
+// Large T favours G = 8 (fewest tile switches); small T, where the partials
+// weigh more, favours smaller G.
 BwdPlan bwd_plan(int64_t T, int64_t nC) {
   BwdPlan p{};
   p.ntt = int((T + kBwdBT - 1) / kBwdBT);
   p.nkc = int(nC / kBwdBK);
   const int sms = device_sms();
-  int64_t best_cost = -1;
+  double best_cost = -1.0;
   for (int G = kBwdMaxG; G >= 1; G >>= 1) {
     if (p.nkc % G) continue;
     const int ngroups = p.nkc / G;
@@ -437,7 +442,9 @@ BwdPlan bwd_plan(int64_t T, int64_t nC) {
     if (grid > sms) grid = sms;
     if (grid < ngroups) continue;  // every group needs a CTA
     const int base = int(grid / ngroups);
-    const int64_t cost = int64_t(G) * ((p.ntt + base - 1) / base);
+    const int64_t tiles = (p.ntt + base - 1) / base;
+    const double part_us = double(grid) * G * kND * kBwdBK * 4 * 2 / 6.0e6;
+    const double cost = 1.56 * double(G * tiles) + 0.28 * double(tiles) + part_us;
     if (best_cost < 0 || cost < best_cost) {
       best_cost = cost;
       p.G = G;
