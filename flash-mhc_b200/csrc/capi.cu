@@ -127,6 +127,23 @@ int fmhc_mhc_grad_x_combine(const void *gx1, const void *grad_li, const float *h
   return check_launch(w);
 }
 
+int fmhc_mhc_grad_x_combine_post(const void *gx1, const void *grad_li, const float *h_pre,
+                                 const void *grad_out, const float *H, void *grad_x, int64_t T,
+                                 int64_t n, int64_t C, void *stream) {
+  const char *w = "fmhc_mhc_grad_x_combine_post";
+  if (int e = check_streams(w, T, n, C)) return e;
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, gx1); FMHC_REQUIRE_PTR(w, grad_li); FMHC_REQUIRE_PTR(w, h_pre);
+  FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, H); FMHC_REQUIRE_PTR(w, grad_x);
+  FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, H);
+  FMHC_REQUIRE_ALIGN2(w, gx1); FMHC_REQUIRE_ALIGN2(w, grad_li); FMHC_REQUIRE_ALIGN2(w, grad_out);
+  FMHC_REQUIRE_ALIGN2(w, grad_x);
+  const int vec = pick_vec(C, {gx1, grad_li, grad_out, grad_x});
+  fmhc::launch_grad_x_combine_post(gx1, grad_li, h_pre, grad_out, H, grad_x, T, int(C), vec,
+                                   (cudaStream_t)stream);
+  return check_launch(w);
+}
+
 int fmhc_k4_fwd(const void *x, const void *lo, const float *H, const float *h_post, void *out,
                 int64_t T, int64_t n, int64_t C, void *stream) {
   const char *w = "fmhc_k4_fwd";
@@ -148,13 +165,15 @@ int fmhc_k4_bwd(const void *grad_out, const void *x, const void *lo, const float
   if (int e = check_streams(w, T, n, C)) return e;
   if (T == 0) return ok();
   FMHC_REQUIRE_PTR(w, grad_out); FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, lo);
-  FMHC_REQUIRE_PTR(w, H); FMHC_REQUIRE_PTR(w, h_post); FMHC_REQUIRE_PTR(w, grad_x);
+  FMHC_REQUIRE_PTR(w, H); FMHC_REQUIRE_PTR(w, h_post);
   FMHC_REQUIRE_PTR(w, grad_lo); FMHC_REQUIRE_PTR(w, grad_H); FMHC_REQUIRE_PTR(w, grad_hp);
   FMHC_REQUIRE_ALIGN16(w, H); FMHC_REQUIRE_ALIGN16(w, h_post);
   FMHC_REQUIRE_ALIGN16(w, grad_H); FMHC_REQUIRE_ALIGN16(w, grad_hp);
   FMHC_REQUIRE_ALIGN2(w, grad_out); FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, lo);
-  FMHC_REQUIRE_ALIGN2(w, grad_x); FMHC_REQUIRE_ALIGN2(w, grad_lo);
-  const int vec = pick_vec(C, {grad_out, x, lo, grad_x, grad_lo});
+  FMHC_REQUIRE_ALIGN2(w, grad_lo);
+  if (grad_x) FMHC_REQUIRE_ALIGN2(w, grad_x);  // NULL: parameter gradients only
+  const int vec = grad_x ? pick_vec(C, {grad_out, x, lo, grad_x, grad_lo})
+                         : pick_vec(C, {grad_out, x, lo, grad_lo});
   fmhc::launch_k4_bwd(grad_out, x, lo, H, h_post, grad_x, grad_lo, grad_H, grad_hp, T, int(C),
                       vec, (cudaStream_t)stream);
   return check_launch(w);

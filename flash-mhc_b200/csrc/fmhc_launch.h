@@ -19,6 +19,9 @@ void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *h
                    int64_t T, int C, int vec, cudaStream_t s);
 void launch_grad_x_combine(const void *gx1, const void *gli, const float *hp, const void *gx4,
                            void *gx, int64_t T, int C, int vec, cudaStream_t s);
+void launch_grad_x_combine_post(const void *gx1, const void *gli, const float *hp,
+                                const void *go, const float *H, void *gx, int64_t T, int C,
+                                int vec, cudaStream_t s);
 void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H,
                    const float *hp, void *gx, void *glo, float *gH, float *ghp, int64_t T,
                    int C, int vec, cudaStream_t s);

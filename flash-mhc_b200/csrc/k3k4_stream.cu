@@ -210,7 +210,9 @@ k4_fwd_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ lo,
 }
 
 // --------------------------------------------------------------- K4 backward
-template <int VEC, int U, int MINB>
+// WITH_GX = false computes only grad_lo, grad_H and grad_h_post (the fused
+// block forms K4's grad_x later, inside its grad_x combination).
+template <int VEC, int U, int MINB, bool WITH_GX>
 __global__ void __launch_bounds__(256, MINB)
 k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const bf16 *__restrict__ lo, const float4 *__restrict__ H,
@@ -234,7 +236,7 @@ k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
     const bf16 *gor = go + t * 4 * C;
     const bf16 *xr = x + t * 4 * C;
     const bf16 *lor = lo + t * C;
-    bf16 *gxr = gx + t * 4 * C;
+    bf16 *gxr = WITH_GX ? gx + t * 4 * C : nullptr;
     bf16 *glor = glo + t * C;
     float accH[16];  // accH[i*4+j] = sum_c go_i * x_j
     float accP[4];   // accP[i]     = sum_c go_i * lo
@@ -282,14 +284,16 @@ k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
             unpack(a[u][j], fx);
 #pragma unroll
             for (int e = 0; e < VEC; ++e) {
-              float s = Hm[0][j] * fg[0][e];
-              s = fmaf(Hm[1][j], fg[1][e], s);
-              s = fmaf(Hm[2][j], fg[2][e], s);
-              o[e] = fmaf(Hm[3][j], fg[3][e], s);
+              if constexpr (WITH_GX) {
+                float s = Hm[0][j] * fg[0][e];
+                s = fmaf(Hm[1][j], fg[1][e], s);
+                s = fmaf(Hm[2][j], fg[2][e], s);
+                o[e] = fmaf(Hm[3][j], fg[3][e], s);
+              }
 #pragma unroll
               for (int i = 0; i < 4; ++i) accH[i * 4 + j] = fmaf(fg[i][e], fx[e], accH[i * 4 + j]);
             }
-            store_stream<VEC>(gxr + j * C + c * VEC, o);
+            if constexpr (WITH_GX) store_stream<VEC>(gxr + j * C + c * VEC, o);
           }
         }
       }
@@ -302,14 +306,19 @@ k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
 }
 
 // ------------------------------------------ combined grad_x of the block
-// gx[t,j,c] = bf16( gx1[t,j,c] + h_pre[t,j] * g_li[t,c] + gx4[t,j,c] )
+// gx[t,j,c] = bf16( gx1[t,j,c] + h_pre[t,j] * g_li[t,c] + k4[t,j,c] )
 // The three contributions to the gradient of the residual streams (K1's
-// backward, K3's grad_x, K4's grad_x) in one pass; gx4 may be null.
-template <int VEC, int U>
+// backward, K3's grad_x, K4's grad_x) in one pass.  MODE selects K4's term:
+//   0: none;
+//   1: k4 = gx4, K4's grad_x as written by its backward kernel (bf16);
+//   2: k4 = sum_i H[t,i,j] * go[t,i,c], formed here from K4's upstream
+//      gradient go (T, 4, C) and H_merged, in f32 and in the order K4's
+//      backward uses, so K4's backward need not write its grad_x at all.
+template <int VEC, int U, int MODE>
 __global__ void __launch_bounds__(256)
 grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli,
-                      const float4 *__restrict__ hp, const bf16 *__restrict__ gx4,
-                      bf16 *__restrict__ gx, int64_t T, int C) {
+                      const float4 *__restrict__ hp, const bf16 *__restrict__ k4,
+                      const float4 *__restrict__ H, bf16 *__restrict__ gx, int64_t T, int C) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
@@ -318,6 +327,14 @@ grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli
   for (int64_t t = warp; t < T; t += nwarps) {
     const float4 h = __ldg(hp + t);
     const float hj[4] = {h.x, h.y, h.z, h.w};
+    float Hm[4][4];
+    if constexpr (MODE == 2) {
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        const float4 r = __ldg(H + t * 4 + i);
+        Hm[i][0] = r.x; Hm[i][1] = r.y; Hm[i][2] = r.z; Hm[i][3] = r.w;
+      }
+    }
     const int64_t row = t * 4 * C;
     for (int c0 = lane; c0 < nchunk; c0 += 32 * U) {
       Chunk<VEC> g[U], a[U][4], b[U][4];
@@ -329,7 +346,7 @@ grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             a[u][j] = ld_raw<VEC>(gx1 + row + j * C + c * VEC);
-            if (gx4) b[u][j] = ld_raw<VEC>(gx4 + row + j * C + c * VEC);
+            if constexpr (MODE != 0) b[u][j] = ld_raw<VEC>(k4 + row + j * C + c * VEC);
           }
         }
       }
@@ -339,15 +356,29 @@ grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli
         if (c < nchunk) {
           float fg[VEC];
           unpack(g[u], fg);
+          float fo[4][VEC];  // MODE 2: the four go rows
+          if constexpr (MODE == 2) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) unpack(b[u][i], fo[i]);
+          }
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             float fa[VEC], o[VEC];
             unpack(a[u][j], fa);
-            if (gx4) {
+            if constexpr (MODE == 1) {
               float fb[VEC];
               unpack(b[u][j], fb);
 #pragma unroll
               for (int e = 0; e < VEC; ++e) o[e] = fmaf(hj[j], fg[e], fa[e] + fb[e]);
+            } else if constexpr (MODE == 2) {
+#pragma unroll
+              for (int e = 0; e < VEC; ++e) {
+                float s4 = Hm[0][j] * fo[0][e];
+                s4 = fmaf(Hm[1][j], fo[1][e], s4);
+                s4 = fmaf(Hm[2][j], fo[2][e], s4);
+                s4 = fmaf(Hm[3][j], fo[3][e], s4);
+                o[e] = fmaf(hj[j], fg[e], fa[e] + s4);
+              }
             } else {
 #pragma unroll
               for (int e = 0; e < VEC; ++e) o[e] = fmaf(hj[j], fg[e], fa[e]);
@@ -439,9 +470,28 @@ void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *h
 void launch_grad_x_combine(const void *gx1, const void *gli, const float *hp, const void *gx4,
                            void *gx, int64_t T, int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
-    auto k = grad_x_combine_kernel<VEC, 2>;
+    if (gx4) {
+      auto k = grad_x_combine_kernel<VEC, 2, 1>;
+      launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
+             (const bf16 *)gli, (const float4 *)hp, (const bf16 *)gx4, (const float4 *)nullptr,
+             (bf16 *)gx, T, C);
+    } else {
+      auto k = grad_x_combine_kernel<VEC, 2, 0>;
+      launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
+             (const bf16 *)gli, (const float4 *)hp, (const bf16 *)nullptr, (const float4 *)nullptr,
+             (bf16 *)gx, T, C);
+    }
+  });
+}
+
+void launch_grad_x_combine_post(const void *gx1, const void *gli, const float *hp,
+                                const void *go, const float *H, void *gx, int64_t T, int C,
+                                int vec, cudaStream_t s) {
+  FMHC_DISPATCH_VEC(vec, {
+    auto k = grad_x_combine_kernel<VEC, 2, 2>;
     launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
-           (const bf16 *)gli, (const float4 *)hp, (const bf16 *)gx4, (bf16 *)gx, T, C);
+           (const bf16 *)gli, (const float4 *)hp, (const bf16 *)go, (const float4 *)H,
+           (bf16 *)gx, T, C);
   });
 }
 
@@ -449,10 +499,17 @@ void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H
                    const float *hp, void *gx, void *glo, float *gH, float *ghp, int64_t T,
                    int C, int vec, cudaStream_t s) {
   FMHC_DISPATCH_VEC(vec, {
-    auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB>;
-    launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
-           (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)gx,
-           (bf16 *)glo, gH, ghp, T, C);
+    if (gx) {
+      auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB, true>;
+      launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
+             (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp,
+             (bf16 *)gx, (bf16 *)glo, gH, ghp, T, C);
+    } else {
+      auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB, false>;
+      launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
+             (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp,
+             (bf16 *)nullptr, (bf16 *)glo, gH, ghp, T, C);
+    }
   });
 }
 

@@ -37,6 +37,7 @@ _SIGNATURES = {
     "fmhc_k3_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k3_bwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_mhc_grad_x_combine": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "fmhc_mhc_grad_x_combine_post": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k4_fwd": [_vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k4_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
 }

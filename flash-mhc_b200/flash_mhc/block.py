@@ -39,18 +39,21 @@ from . import ops as _ops  # noqa: F401  (registers torch.ops.flash_mhc.*)
 
 
 class _StreamGrad:
-    """Hands K4's grad_x from the post-res backward to the pre-map backward.
+    """Hands K4's share of grad_x from the post-res backward to the pre-map backward.
 
-    The post-res backward always runs first (the pre-map's outputs feed it),
-    so instead of returning its grad_x to the autograd engine, which would add
-    it to the pre-map's grad_x with a separate full pass, it parks the tensor
-    here and the pre-map backward folds it into its one combining pass.
+    The post-res backward always runs first (the pre-map's outputs feed it).
+    Instead of writing K4's grad_x (sum_i H[i, j] * g_out[i]) and returning it
+    to the autograd engine, which would add it to the pre-map's grad_x with a
+    separate full pass, it parks K4's upstream gradient and H_merged here, and
+    the pre-map backward forms K4's term inside its one combining pass: one
+    (T, n, C) write and one read fewer.
     """
 
-    __slots__ = ("gx4",)
+    __slots__ = ("g_out", "H")
 
     def __init__(self):
-        self.gx4 = None
+        self.g_out = None
+        self.H = None
 
 
 class _FusedPreMap(torch.autograd.Function):
@@ -58,7 +61,8 @@ class _FusedPreMap(torch.autograd.Function):
 
     Backward from saved tensors only (no forward kernel is re-run):
     K3's grad_h_pre -> K2 bwd -> K1 bwd (grad_x and grad_W in one pass), then
-    one pass forming grad_x = K1's + h_pre * grad_layer_input + K4's.
+    one pass forming grad_x = K1's + h_pre * grad_layer_input + K4's, K4's
+    term computed there from the block's output gradient and H_merged.
     """
 
     @staticmethod
@@ -85,8 +89,12 @@ class _FusedPreMap(torch.autograd.Function):
             g_hpre, z(T, 4) if g_hpost is None else g_hpost, z(T, 4, 4) if g_H is None else g_H,
             proj, a_pre, a_post, a_res, bias, perm)
         gx1, gW = ops.fused_rmsnorm_project_backward(g_proj, x.reshape(T, n * C), W, proj, inv)
-        gx4, ctx.slot.gx4 = ctx.slot.gx4, None
-        gx = ops.mhc_grad_x_combine(gx1.view(T, n, C), g_li, h_pre, gx4)
+        g_out, H = ctx.slot.g_out, ctx.slot.H
+        ctx.slot.g_out = ctx.slot.H = None
+        if g_out is None:
+            gx = ops.mhc_grad_x_combine(gx1.view(T, n, C), g_li, h_pre, None)
+        else:
+            gx = ops.mhc_grad_x_combine_post(gx1.view(T, n, C), g_li, h_pre, g_out, H)
         return (gx, gW, gp[0:1].view_as(a_pre).to(a_pre.dtype),
                 gp[1:2].view_as(a_post).to(a_post.dtype), gp[2:3].view_as(a_res).to(a_res.dtype),
                 gp[3:35].view_as(bias).to(bias.dtype), None, None)
@@ -95,8 +103,9 @@ class _FusedPreMap(torch.autograd.Function):
 class _FusedPostRes(torch.autograd.Function):
     """K4 forward; backward K4 bwd from the saved inputs (the output is not kept).
 
-    K4's grad_x goes to the pre-map backward through ``slot`` (see _StreamGrad);
-    the engine receives None for x from here.
+    The backward computes grad_layer_output, grad_H and grad_h_post only; K4's
+    grad_x is formed by the pre-map backward from what is parked in ``slot``
+    (see _StreamGrad), and the engine receives None for x from here.
     """
 
     @staticmethod
@@ -108,8 +117,9 @@ class _FusedPostRes(torch.autograd.Function):
     @staticmethod
     def backward(ctx, g_out):
         x, lo, H, hp = ctx.saved_tensors
-        gx4, glo, gH, ghp = torch.ops.flash_mhc.fused_post_res_backward(g_out, x, lo, H, hp)
-        ctx.slot.gx4 = gx4
+        g_out = g_out.contiguous()
+        glo, gH, ghp = torch.ops.flash_mhc.post_res_grad_params(g_out, x, lo, H, hp)
+        ctx.slot.g_out, ctx.slot.H = g_out, H
         return None, glo, gH, ghp, None
 
 

@@ -57,6 +57,14 @@ _lib.define("pre_map_grad_h(Tensor grad_out, Tensor x_streams, Tensor h_pre) -> 
 _lib.define(
     "mhc_grad_x_combine(Tensor gx1, Tensor grad_layer_input, Tensor h_pre, Tensor? gx4) -> Tensor grad_x"
 )
+# K4 backward without its grad_x, and the combination that forms K4's grad_x
+# from K4's upstream gradient instead (one (T, n, C) write and read fewer).
+_lib.define(
+    "post_res_grad_params(Tensor grad_out, Tensor x_streams, Tensor layer_output, Tensor H_merged, Tensor h_post) -> (Tensor grad_layer_output, Tensor grad_H_merged, Tensor grad_h_post)"
+)
+_lib.define(
+    "mhc_grad_x_combine_post(Tensor gx1, Tensor grad_layer_input, Tensor h_pre, Tensor grad_out, Tensor H_merged) -> Tensor grad_x"
+)
 _lib.define(
     "mhc_coeffs_backward(Tensor grad_h_pre, Tensor grad_h_post, Tensor grad_H_merged, Tensor proj, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor grad_proj, Tensor grad_params)"
 )
@@ -135,6 +143,19 @@ def _pre_map_grad_h_fake(grad_out, x_streams, h_pre):
 
 @torch.library.register_fake("flash_mhc::mhc_grad_x_combine")
 def _mhc_grad_x_combine_fake(gx1, grad_layer_input, h_pre, gx4):
+    return torch.empty_like(gx1)
+
+
+@torch.library.register_fake("flash_mhc::post_res_grad_params")
+def _post_res_grad_params_fake(grad_out, x_streams, layer_output, H_merged, h_post):
+    T, n, C = x_streams.shape
+    return (x_streams.new_empty((T, C)),
+            x_streams.new_empty((T, n, n), dtype=torch.float32),
+            x_streams.new_empty((T, n), dtype=torch.float32))
+
+
+@torch.library.register_fake("flash_mhc::mhc_grad_x_combine_post")
+def _mhc_grad_x_combine_post_fake(gx1, grad_layer_input, h_pre, grad_out, H_merged):
     return torch.empty_like(gx1)
 
 
@@ -359,6 +380,43 @@ def _mhc_grad_x_combine_cuda(gx1, grad_layer_input, h_pre, gx4):
                      None if gx4 is None else gx4.data_ptr(), grad_x.data_ptr(), T, n, C,
                      _stream(gx1))
     return grad_x
+
+
+@torch.library.impl(_lib, "mhc_grad_x_combine_post", "CUDA")
+def _mhc_grad_x_combine_post_cuda(gx1, grad_layer_input, h_pre, grad_out, H_merged):
+    T, n, C = gx1.shape
+    _n4("mhc_grad_x_combine_post", n)
+    gx1 = _bf16("gx1", gx1)
+    gli = _bf16("grad_layer_input", grad_layer_input)
+    h_pre = _coef(h_pre)
+    grad_out = _bf16("grad_out", grad_out)
+    H_merged = _coef(H_merged)
+    grad_x = torch.empty_like(gx1)
+    with _on_device(gx1):
+        _native.call("fmhc_mhc_grad_x_combine_post", gx1.data_ptr(), gli.data_ptr(),
+                     h_pre.data_ptr(), grad_out.data_ptr(), H_merged.data_ptr(),
+                     grad_x.data_ptr(), T, n, C, _stream(gx1))
+    return grad_x
+
+
+@torch.library.impl(_lib, "post_res_grad_params", "CUDA")
+def _post_res_grad_params_cuda(grad_out, x_streams, layer_output, H_merged, h_post):
+    T, n, C = x_streams.shape
+    _n4("post_res_grad_params", n)
+    grad_out = _bf16("grad_out", grad_out)
+    x_streams = _bf16("x_streams", x_streams)
+    layer_output = _bf16("layer_output", layer_output)
+    H_merged = _coef(H_merged)
+    h_post = _coef(h_post)
+    grad_layer_output = torch.empty((T, C), device=x_streams.device, dtype=x_streams.dtype)
+    grad_H = torch.empty((T, n, n), device=x_streams.device, dtype=torch.float32)
+    grad_hp = torch.empty((T, n), device=x_streams.device, dtype=torch.float32)
+    with _on_device(x_streams):
+        _native.call("fmhc_k4_bwd", grad_out.data_ptr(), x_streams.data_ptr(),
+                     layer_output.data_ptr(), H_merged.data_ptr(), h_post.data_ptr(),
+                     None, grad_layer_output.data_ptr(), grad_H.data_ptr(),
+                     grad_hp.data_ptr(), T, n, C, _stream(x_streams))
+    return grad_layer_output, grad_H, grad_hp
 
 
 @torch.library.impl(_lib, "fused_post_res", "CUDA")

@@ -173,6 +173,9 @@ FMHC_API int fmhc_k4_fwd(const void *x, const void *lo, const float *H,
  *   grad_hp[t,i]  = sum_c go[t,i,c] * lo[t,c]                        (f32)
  *   grad_H[t,i,j] = sum_c go[t,i,c] * x[t,j,c]                       (f32)
  *   grad_x[t,j,c] = bf16( sum_i H[t,i,j] * go[t,i,c] )
+ * grad_x may be NULL: then only grad_lo, grad_hp and grad_H are computed and
+ * one (T, n, C) write is saved (fmhc_mhc_grad_x_combine_post forms K4's
+ * grad_x later from go and H).
  * Replaces op flash_mhc::fused_post_res_backward (src/flash_mhc/ops.py:39-41,
  * 570-667) and kernel _fused_post_res_bwd_fused_kernel_n4
  * (src/flash_mhc/kernels.py:487-665).
@@ -194,6 +197,21 @@ FMHC_API int fmhc_k4_bwd(const void *grad_out, const void *x, const void *lo,
 FMHC_API int fmhc_mhc_grad_x_combine(const void *gx1, const void *grad_li, const float *h_pre,
                                      const void *gx4, void *grad_x, int64_t T, int64_t n,
                                      int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
+ * The same combination with K4's grad_x formed in place from K4's upstream
+ * gradient instead of read back:
+ *   grad_x[t,j,c] = bf16( gx1[t,j,c] + h_pre[t,j] * grad_li[t,c]
+ *                         + sum_i H[t,i,j] * grad_out[t,i,c] )
+ * grad_out: the gradient of the block output (T, n, C) bf16; H: H_merged
+ * (T, n, n) f32.  With fmhc_k4_bwd(grad_x = NULL) this saves K4's (T, n, C)
+ * grad_x write and its read here.  grad_x may alias gx1.
+ * No counterpart in the reference (its autograd engine sums three tensors).
+ */
+FMHC_API int fmhc_mhc_grad_x_combine_post(const void *gx1, const void *grad_li,
+                                          const float *h_pre, const void *grad_out,
+                                          const float *H, void *grad_x, int64_t T, int64_t n,
+                                          int64_t C, void *stream);
 
 /* ------------------------------------------------------------------------
  * K2 forward: the per-token coefficient math on the 32 projection logits

@@ -334,6 +334,18 @@ def test_block_backward_pieces(T, C):
             ref = ref + extra.float()
         torch.testing.assert_close(out.float(), ref, atol=BF_ATOL, rtol=BF_RTOL)
 
+    # K4 backward without grad_x gives the other three gradients bit for bit,
+    # and the combination forms K4's grad_x term from g_out and H itself.
+    lo, H, hpost, g_out = _bf(d["lo"]), _f32(d["H"]), _f32(d["hpost"]), _bf(d["g_post"])
+    k4_ref = torch.ops.flash_mhc.fused_post_res_backward(g_out, x, lo, H, hpost)
+    k4 = torch.ops.flash_mhc.post_res_grad_params(g_out, x, lo, H, hpost)
+    for got, want in zip(k4, k4_ref[1:]):
+        assert torch.equal(got, want)
+    out = torch.ops.flash_mhc.mhc_grad_x_combine_post(gx1, gli, hp, g_out, H)
+    ref = (gx1.float() + hp[:, :, None] * gli.float()[:, None, :]
+           + torch.einsum("tij,tic->tjc", H, g_out.float()))
+    torch.testing.assert_close(out.float(), ref, atol=BF_ATOL, rtol=BF_RTOL)
+
 
 def test_large_token_sharded_config_rows():
     """The large per-GPU config (131,072 tokens x C = 4096: every (T, 4, C)
