@@ -316,6 +316,9 @@ def run_ours(args):
     # --- small per-GPU batch: eager vs CUDA-graph replay -------------------
     graphs = None if args.no_graphs else run_small_graphs(args, torch, dev)
 
+    # --- tiny-T no-grad inference latency (BASELINE configs[4] shapes) -------
+    tiny = None if (args.no_tiny or world > 1) else run_tiny_inference(args, torch, dev)
+
     if rank == 0:
         peaks = measured_peaks()
         bm = bytes_model(T, C)
@@ -357,6 +360,7 @@ def run_ours(args):
             "e2e": e2e,
             "block": block,
             "small_batch_graphs": graphs,
+            "tiny_inference": tiny,
             "gpu_launches": HotPath.LAUNCHES_PER_STEP * args.steps,
             "clocks": clk.summary(),
             "native_lib": os.path.relpath(lib_path, ROOT),
@@ -378,6 +382,68 @@ def _physical_gpu_indices(world):
         except ValueError:
             pass
     return list(range(world))
+
+
+def run_tiny_inference(args, torch, dev):
+    """Latency of one no-grad MHCLiteBlock forward at tiny token counts
+    (T in {1, 16, 256}, C = 768, n = 4 bf16, x ~N(0,1)
+    with 1% of channels x100, projection weights ~N(0,0.02), wrapped
+    768 -> 768 bias-free linear), eager and replayed from a CUDA graph.
+    Microseconds per forward, averaged over 200 back-to-back calls."""
+    import torch.nn as nn
+
+    from flash_mhc import MHCLiteBlock
+
+    C = 768
+    g = torch.Generator(device=dev)
+    g.manual_seed(123)
+    layer = nn.Linear(C, C, bias=False)
+    blk = MHCLiteBlock(4, C, layer).to(dev).to(torch.bfloat16).eval()
+    with torch.no_grad():
+        blk.W_all.weight.copy_(torch.randn(blk.W_all.weight.shape, generator=g, device=dev) * 0.02)
+        layer.weight.copy_(torch.randn(C, C, generator=g, device=dev) * 0.02)
+    cols = torch.randperm(C, generator=torch.Generator().manual_seed(5))[: C // 100].to(dev)
+    n = 200
+    out = {}
+    for T in (1, 16, 256):
+        x = torch.randn(T, N_STREAMS, C, generator=g, device=dev)
+        x[:, :, cols] *= 100.0
+        x = x.bfloat16()
+
+        def fwd():
+            with torch.no_grad():
+                return blk(x)
+
+        def timed(fn):
+            for _ in range(10):
+                fn()
+            torch.cuda.synchronize()
+            s = torch.cuda.Event(enable_timing=True)
+            e = torch.cuda.Event(enable_timing=True)
+            s.record()
+            for _ in range(n):
+                fn()
+            e.record()
+            torch.cuda.synchronize()
+            return s.elapsed_time(e) / n * 1e3
+
+        eager_us = timed(fwd)
+        side = torch.cuda.Stream()
+        side.wait_stream(torch.cuda.current_stream())
+        with torch.cuda.stream(side):
+            for _ in range(2):
+                fwd()
+        torch.cuda.current_stream().wait_stream(side)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph):
+            fwd()
+        graph_us = timed(graph.replay)
+        del graph
+        out[str(T)] = {"eager_us": round(eager_us, 2), "graph_us": round(graph_us, 2)}
+    return {"config": {"workload": "MHCLiteBlock no-grad forward (configs[4] tiny-T shapes)",
+                       "C": C, "n": N_STREAMS, "layer": "nn.Linear(768, 768, bias=False)",
+                       "x": "N(0,1), 1% of channels x100"},
+            "calls": n, "latency_per_forward": out}
 
 
 def run_small_graphs(args, torch, dev):
@@ -787,6 +853,7 @@ def main():
     ap.add_argument("--block-T", type=int, default=65536, help="tokens per GPU for the block")
     ap.add_argument("--block-C", type=int, default=2048)
     ap.add_argument("--no-graphs", action="store_true", help="skip the small-batch graph measurement")
+    ap.add_argument("--no-tiny", action="store_true", help="skip the tiny-T inference latency")
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer e2e leg (its pinned buffers grow with --T/--C)")
     ap.add_argument("--small-T", type=int, default=8192)

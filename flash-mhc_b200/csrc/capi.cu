@@ -199,7 +199,11 @@ int fmhc_k1_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t
   FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, W); FMHC_REQUIRE_ALIGN2(w, out);
   if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
   cudaStream_t s = (cudaStream_t)stream;
-  if (fmhc::k1_tc_fwd_supported(x, W, out, inv_rms, T, nC, D)) {
+  if (T <= FMHC_K1_ROWS_MAX_T && D == 32 && nC % 8 == 0 && aligned(x, 16) && aligned(W, 16)) {
+    // Few tokens: one pass over W per block of 4 tokens beats the tensor-core
+    // kernel's serial k-loop per tile.
+    fmhc::launch_k1_fwd_rows(x, W, out, inv_rms, T, int(nC), int(D), s);
+  } else if (fmhc::k1_tc_fwd_supported(x, W, out, inv_rms, T, nC, D)) {
     if (int e = fmhc::launch_k1_tc_fwd(x, W, out, inv_rms, T, int(nC), s))
       return fail(e, "%s: %s", w, fmhc::k1_tc_error());
   } else {

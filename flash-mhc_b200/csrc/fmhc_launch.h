@@ -29,6 +29,17 @@ void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H
 // k1_simt.cu -- general-shape K1 (vec is 8 or 1).
 void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
                         int nC, int D, int vec, cudaStream_t s);
+// Small-T forward (block per 2 tokens, k split over the block); D == 32,
+// nC % 8 == 0, x and W 16-byte aligned.
+void launch_k1_fwd_rows(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
+                        int nC, int D, cudaStream_t s);
+// Largest T for which fmhc_k1_fwd takes the small-T kernel: three waves of
+// its one-block-per-SM grid on 148 SMs.  Measured at nC = 3072 (4096): 5.4
+// (6.1) us up to T = 256, 10.2 (11.8) us at 512, 18.9 (22.0) us at 1024,
+// against 18.6 (23.7) us for the tensor-core kernel at any T below ~9000.
+#ifndef FMHC_K1_ROWS_MAX_T
+#define FMHC_K1_ROWS_MAX_T 888
+#endif
 void launch_k1_bwd_dx_simt(const void *go, const void *x, const void *W, const void *proj,
                            const float *inv_rms, void *gx, int64_t T, int nC, int D, int vec,
                            cudaStream_t s);

@@ -70,6 +70,107 @@ k1_fwd_simt_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
   }
 }
 
+// Small-T forward.  One block of 256 threads per 2 tokens; the threads split
+// the nC columns into 16-byte chunks (chunk c belongs to thread c mod 256) and
+// each accumulates, over its chunks, both tokens' sums of squares and 32 dot
+// products with W.  The block then reduces them: a warp butterfly per value,
+// then the 8 warp totals are added in warp order in shared memory.  A tile of
+// the tensor-core kernel walks its nC / 64 k-steps one after another, ~18 us
+// at nC = 3072 whatever T; here every block makes one pass over W.
+// Needs D == 32, nC % 8 == 0 and 16-byte aligned x and W.
+constexpr int kRowsTB = 2;
+__global__ void __launch_bounds__(256, 1)
+k1_fwd_rows_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
+                   bf16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T, int nC,
+                   int D) {
+  pdl_wait();
+  __shared__ float red[8][kRowsTB][33];
+  __shared__ float tot[kRowsTB][33];
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int64_t t0 = int64_t(blockIdx.x) * kRowsTB;
+  const bool has1 = t0 + 1 < T;
+  const int nchunk = nC / 8;
+  float acc0[32], acc1[32], ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+  for (int d = 0; d < 32; ++d) acc0[d] = acc1[d] = 0.f;
+  for (int c = tid; c < nchunk; c += 256) {
+    const uint4 u0 = __ldcs(reinterpret_cast<const uint4 *>(x + t0 * nC + c * 8));
+    uint4 u1 = make_uint4(0u, 0u, 0u, 0u);
+    if (has1) u1 = __ldcs(reinterpret_cast<const uint4 *>(x + (t0 + 1) * nC + c * 8));
+    const float f0[8] = {bf16lo(u0.x), bf16hi(u0.x), bf16lo(u0.y), bf16hi(u0.y),
+                         bf16lo(u0.z), bf16hi(u0.z), bf16lo(u0.w), bf16hi(u0.w)};
+    const float f1[8] = {bf16lo(u1.x), bf16hi(u1.x), bf16lo(u1.y), bf16hi(u1.y),
+                         bf16lo(u1.z), bf16hi(u1.z), bf16lo(u1.w), bf16hi(u1.w)};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ss0 = fmaf(f0[e], f0[e], ss0);
+      ss1 = fmaf(f1[e], f1[e], ss1);
+    }
+    // W rows in two batches of 16 loads, all in flight before their FMAs
+    // (loads behind a per-row condition were issued one round trip at a time).
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      uint4 wv[16];
+#pragma unroll
+      for (int i = 0; i < 16; ++i)
+        wv[i] = __ldg(reinterpret_cast<const uint4 *>(W + int64_t(16 * h + i) * nC + c * 8));
+#pragma unroll
+      for (int i = 0; i < 16; ++i) {
+        const uint4 u = wv[i];
+        const float fw[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
+                             bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+        const int d = 16 * h + i;
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          acc0[d] = fmaf(f0[e], fw[e], acc0[d]);
+          acc1[d] = fmaf(f1[e], fw[e], acc1[d]);
+        }
+      }
+    }
+  }
+  // Butterfly per value: with two 32-value reduce-scatters the accumulators
+  // were placed in local memory.
+#pragma unroll
+  for (int d = 0; d < 32; ++d)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      acc0[d] += __shfl_xor_sync(0xffffffffu, acc0[d], off);
+      acc1[d] += __shfl_xor_sync(0xffffffffu, acc1[d], off);
+    }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    ss0 += __shfl_xor_sync(0xffffffffu, ss0, off);
+    ss1 += __shfl_xor_sync(0xffffffffu, ss1, off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int d = 0; d < 32; ++d) {
+      red[warp][0][d] = acc0[d];
+      red[warp][1][d] = acc1[d];
+    }
+    red[warp][0][32] = ss0;
+    red[warp][1][32] = ss1;
+  }
+  __syncthreads();
+  if (tid < kRowsTB * 33) {
+    const int tb = tid / 33, j = tid - tb * 33;
+    float v = red[0][tb][j];
+#pragma unroll
+    for (int w = 1; w < 8; ++w) v += red[w][tb][j];
+    tot[tb][j] = v;
+  }
+  __syncthreads();
+  if (tid < kRowsTB * 32) {
+    const int tb = tid / 32, d = tid - tb * 32;
+    const int64_t t = t0 + tb;
+    if (t < T) {
+      const float r = rsqrtf(tot[tb][32] / float(nC) + kK1Eps);
+      out[t * 32 + d] = __float2bfloat16_rn(tot[tb][d] * r);
+      if (d == 0) inv_rms[t] = r;
+    }
+  }
+}
+
 template <int VEC>
 __global__ void __launch_bounds__(256)
 k1_bwd_dx_simt_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
@@ -218,6 +319,12 @@ void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms,
   else
     launch(k1_fwd_simt_kernel<1>, dim3(warp_grid(T)), dim3(256), 0, s, (const bf16 *)x,
            (const bf16 *)W, (bf16 *)out, inv_rms, T, nC, D);
+}
+
+void launch_k1_fwd_rows(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
+                        int nC, int D, cudaStream_t s) {
+  launch(k1_fwd_rows_kernel, dim3(unsigned((T + kRowsTB - 1) / kRowsTB)), dim3(256), 0, s,
+         (const bf16 *)x, (const bf16 *)W, (bf16 *)out, inv_rms, T, nC, D);
 }
 
 void launch_k1_bwd_dx_simt(const void *go, const void *x, const void *W, const void *proj,

@@ -261,11 +261,14 @@ def test_metric_shape_runs_the_tensor_core_k1():
 
 @pytest.mark.parametrize("T,C", [(1, 256), (31, 256), (33, 256), (1000, 256), (4733, 256),
                                  (3000, 1024), (129, 2048),
-                                 (65536, 64)])  # 2 k-chunks: ~74 CTAs add into each
+                                 (65536, 64),   # 2 k-chunks: 74 CTAs add into each
+                                 (20000, 1024),  # groups of 4 k-chunks, 18 or 19 CTAs each
+                                 (6000, 768)])  # groups of 2, 12 or 13 CTAs each, nC = 3072
 def test_k1_token_partitioning(T, C):
     """Forward: token ranges split across CTAs in 32-row units, partial tiles.
-    Backward: (k-chunk, token-tile) unit runs per CTA that cross k-chunk
-    segments, fewer units than SMs, partial token tiles; grad_W reduction."""
+    Backward: the k-chunks form groups of G (1, 2, 4 or 8, chosen per shape),
+    each CTA of a group takes every ng-th token tile; groups of unequal CTA
+    counts, fewer tiles than CTAs, partial token tiles; grad_W reduction."""
     d = _inputs(T, C, 40 + T)
     xf_np = d["x"].reshape(T, 4 * C)
     xf, W, go = _bf(xf_np), _bf(d["W"]), _bf(d["g_proj"])
