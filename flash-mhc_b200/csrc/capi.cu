@@ -292,7 +292,35 @@ int fmhc_k2_fwd(const void *proj, const float *params, const float *perm, float 
   FMHC_REQUIRE_ALIGN16(w, proj); FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, h_post);
   FMHC_REQUIRE_ALIGN16(w, H_merged);
   if (!aligned(params, 4) || !aligned(perm, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: params/perm must be 4-byte aligned", w);
-  fmhc::launch_k2_fwd(proj, params, perm, h_pre, h_post, H_merged, T, (cudaStream_t)stream);
+  fmhc::launch_k2_fwd(proj, fmhc::k2_packed_params(params, perm), h_pre, h_post, H_merged, T,
+                      (cudaStream_t)stream);
+  return check_launch(w);
+}
+
+int fmhc_k2_fwd_typed(const void *proj, const void *alpha_pre, const void *alpha_post,
+                      const void *alpha_res, const void *bias, int param_dtype, const void *perm,
+                      int perm_dtype, float *h_pre, float *h_post, float *H_merged, int64_t T,
+                      void *stream) {
+  const char *w = "fmhc_k2_fwd_typed";
+  if (T < 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: T must be >= 0 (got %lld)", w, (long long)T);
+  const auto dt_ok = [](int d) { return d == FMHC_DTYPE_F32 || d == FMHC_DTYPE_BF16; };
+  if (!dt_ok(param_dtype) || !dt_ok(perm_dtype))
+    return fail(FMHC_ERR_UNSUPPORTED, "%s: parameter dtypes must be FMHC_DTYPE_F32 or FMHC_DTYPE_BF16", w);
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, alpha_pre); FMHC_REQUIRE_PTR(w, alpha_post);
+  FMHC_REQUIRE_PTR(w, alpha_res); FMHC_REQUIRE_PTR(w, bias); FMHC_REQUIRE_PTR(w, perm);
+  FMHC_REQUIRE_PTR(w, h_pre); FMHC_REQUIRE_PTR(w, h_post); FMHC_REQUIRE_PTR(w, H_merged);
+  FMHC_REQUIRE_ALIGN16(w, proj); FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, h_post);
+  FMHC_REQUIRE_ALIGN16(w, H_merged);
+  const uintptr_t pa = param_dtype == FMHC_DTYPE_BF16 ? 2 : 4;
+  const uintptr_t qa = perm_dtype == FMHC_DTYPE_BF16 ? 2 : 4;
+  if (!aligned(alpha_pre, pa) || !aligned(alpha_post, pa) || !aligned(alpha_res, pa) ||
+      !aligned(bias, pa) || !aligned(perm, qa))
+    return fail(FMHC_ERR_ALIGNMENT, "%s: parameters must be aligned to their element size", w);
+  const fmhc::K2Params P{alpha_pre, alpha_post, alpha_res, bias, perm,
+                         param_dtype == FMHC_DTYPE_BF16 ? 1 : 0,
+                         perm_dtype == FMHC_DTYPE_BF16 ? 1 : 0};
+  fmhc::launch_k2_fwd(proj, P, h_pre, h_post, H_merged, T, (cudaStream_t)stream);
   return check_launch(w);
 }
 

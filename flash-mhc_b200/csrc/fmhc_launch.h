@@ -50,8 +50,16 @@ void launch_k1_dw_simt(const void *go, const void *x, const float *inv_rms, void
 
 // k2_coeffs.cu -- coefficient math (n = 4, D = 32).
 int64_t k2_bwd_workspace_bytes(int64_t T);
-void launch_k2_fwd(const void *proj, const float *params, const float *perm, float *h_pre,
-                   float *h_post, float *H, int64_t T, cudaStream_t s);
+// The K2 parameters where they live: a_pre, a_post, a_res (one value each),
+// bias (32) and the permutation rows perm (24 x 16), each f32 or bf16.
+struct K2Params {
+  const void *a_pre, *a_post, *a_res, *bias, *perm;
+  int param_bf16, perm_bf16;
+};
+// params (35,) f32 = [a_pre, a_post, a_res, bias[32]], perm (24, 16) f32.
+K2Params k2_packed_params(const float *params, const float *perm);
+void launch_k2_fwd(const void *proj, const K2Params &P, float *h_pre, float *h_post, float *H,
+                   int64_t T, cudaStream_t s);
 void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
                    const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
                    float *ws, int64_t T, cudaStream_t s);

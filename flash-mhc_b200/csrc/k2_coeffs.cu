@@ -40,9 +40,21 @@ struct K2Smem {
   float perm[kNF * 16];
 };
 
-__device__ __forceinline__ void load_params(K2Smem &sm, const float *params, const float *perm) {
-  for (int i = threadIdx.x; i < kP; i += blockDim.x) sm.par[i] = bf16r(params[i]);
-  for (int i = threadIdx.x; i < kNF * 16; i += blockDim.x) sm.perm[i] = bf16r(perm[i]);
+__device__ __forceinline__ float ld_param(const void *p, int i, int is_bf16) {
+  return is_bf16 ? __bfloat162float(reinterpret_cast<const bf16 *>(p)[i])
+                 : reinterpret_cast<const float *>(p)[i];
+}
+
+__device__ __forceinline__ void load_params(K2Smem &sm, const K2Params &P) {
+  for (int i = threadIdx.x; i < kP; i += blockDim.x) {
+    const float v = i == 0 ? ld_param(P.a_pre, 0, P.param_bf16)
+                  : i == 1 ? ld_param(P.a_post, 0, P.param_bf16)
+                  : i == 2 ? ld_param(P.a_res, 0, P.param_bf16)
+                           : ld_param(P.bias, i - 3, P.param_bf16);
+    sm.par[i] = bf16r(v);
+  }
+  for (int i = threadIdx.x; i < kNF * 16; i += blockDim.x)
+    sm.perm[i] = bf16r(ld_param(P.perm, i, P.perm_bf16));
   __syncthreads();
 }
 
@@ -95,16 +107,15 @@ __device__ __forceinline__ void k2_forward_token(const K2Smem &sm, const float (
 }  // namespace
 
 __global__ void __launch_bounds__(256)
-k2_fwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
-              const float *__restrict__ perm, float4 *__restrict__ h_pre,
+k2_fwd_kernel(const bf16 *__restrict__ proj, const K2Params P, float4 *__restrict__ h_pre,
               float4 *__restrict__ h_post, float4 *__restrict__ H, int64_t T) {
   pdl_wait();
   __shared__ K2Smem sm;
-  load_params(sm, params, perm);
   const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
-  if (t >= T) return;
   float v[32];
-  load_proj(proj, t, v);
+  if (t < T) load_proj(proj, t, v);  // in flight while the parameters are staged
+  load_params(sm, P);
+  if (t >= T) return;
   K2Tok k;
   k2_forward_token(sm, v, k);
   float Hm[16];
@@ -125,14 +136,13 @@ k2_fwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
 // One thread per token; each block writes the sums of its tokens' parameter
 // gradients to part[blockIdx.x][35].
 __global__ void __launch_bounds__(256)
-k2_bwd_kernel(const bf16 *__restrict__ proj, const float *__restrict__ params,
-              const float *__restrict__ perm, const float4 *__restrict__ g_hpre,
+k2_bwd_kernel(const bf16 *__restrict__ proj, const K2Params P, const float4 *__restrict__ g_hpre,
               const float4 *__restrict__ g_hpost, const float4 *__restrict__ g_H,
               bf16 *__restrict__ g_proj, float *__restrict__ part, int64_t T) {
   pdl_wait();
   __shared__ K2Smem sm;
   __shared__ float red[8][kP];
-  load_params(sm, params, perm);
+  load_params(sm, P);
   const int64_t t = int64_t(blockIdx.x) * blockDim.x + threadIdx.x;
   float gp[kP];  // this token's contribution to the 35 parameter gradients
 #pragma unroll
@@ -237,19 +247,23 @@ int64_t k2_bwd_workspace_bytes(int64_t T) {
   return ((nb * kP * 4) + 255) & ~int64_t(255);
 }
 
-void launch_k2_fwd(const void *proj, const float *params, const float *perm, float *h_pre,
-                   float *h_post, float *H, int64_t T, cudaStream_t s) {
+K2Params k2_packed_params(const float *params, const float *perm) {
+  return K2Params{params, params + 1, params + 2, params + 3, perm, 0, 0};
+}
+
+void launch_k2_fwd(const void *proj, const K2Params &P, float *h_pre, float *h_post, float *H,
+                   int64_t T, cudaStream_t s) {
   const unsigned nb = unsigned((T + 255) / 256);
-  launch(k2_fwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj, params, perm,
-         (float4 *)h_pre, (float4 *)h_post, (float4 *)H, T);
+  launch(k2_fwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj, P, (float4 *)h_pre,
+         (float4 *)h_post, (float4 *)H, T);
 }
 
 void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
                    const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
                    float *ws, int64_t T, cudaStream_t s) {
   const unsigned nb = unsigned((T + 255) / 256);
-  launch(k2_bwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj, params, perm,
-         (const float4 *)g_hpre, (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj, ws,
+  launch(k2_bwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj,
+         k2_packed_params(params, perm), (const float4 *)g_hpre, (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj, ws,
          T);
   launch(k2_param_reduce_kernel, dim3(kP), dim3(32), 0, s, ws, g_params, int(nb));
 }

@@ -250,7 +250,25 @@ class MHCLiteBlock(nn.Module):
             return torch.ops.flash_mhc.fused_post_res(x_streams, layer_output, H_merged, h_post)
         return _FusedPostRes.apply(x_streams, layer_output, H_merged, h_post, slot)
 
+    def _forward_fused_no_grad(self, x_streams: torch.Tensor, **kwargs) -> torch.Tensor:
+        """Inference (grad disabled, not under torch.compile): the same kernels
+        called without the autograd Functions and the op dispatcher, whose host
+        cost dominates at small T (~200 -> ~70 us per forward at T = 1)."""
+        T = x_streams.shape[0]
+        dt = x_streams.dtype
+        W = self.W_all.weight
+        if W.dtype != dt:
+            W = W.to(dt)
+        proj, _inv = _ops._fused_rmsnorm_project_cuda(x_streams.reshape(T, self.nC), W)
+        h_pre, h_post, H_merged = _ops._mhc_coeffs_cuda(
+            proj, self.alpha_pre, self.alpha_post, self.alpha_res, self.W_all.bias, self.perm_mat)
+        layer_input = _ops._fused_pre_map_cuda(x_streams, h_pre)
+        layer_output = self.layer(layer_input, **kwargs)
+        return _ops._fused_post_res_cuda(x_streams, layer_output, H_merged, h_post)
+
     def _forward_triton(self, x_streams: torch.Tensor, **kwargs) -> torch.Tensor:
+        if not torch.is_grad_enabled() and not torch.compiler.is_compiling():
+            return self._forward_fused_no_grad(x_streams, **kwargs)
         # No torch checkpointing here: the fused autograd functions already keep
         # only the small per-token tensors their backward kernels read.
         slot = _StreamGrad()

@@ -295,15 +295,32 @@ def _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
     return _bf16("proj", proj), params, perm.to(torch.float32).contiguous()
 
 
+_K2_DTYPES = {torch.float32: 0, torch.bfloat16: 1}  # FMHC_DTYPE_F32, FMHC_DTYPE_BF16
+
+
 @torch.library.impl(_lib, "mhc_coeffs", "CUDA")
 def _mhc_coeffs_cuda(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
-    proj, params, perm = _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm)
+    pdt, qdt = _K2_DTYPES.get(bias.dtype), _K2_DTYPES.get(perm.dtype)
+    same = all(a.dtype == bias.dtype for a in (alpha_pre, alpha_post, alpha_res))
+    if pdt is None or qdt is None or not same or proj.dim() != 2 or proj.shape[1] != 32 \
+            or bias.numel() != 32 or perm.shape != (24, 16):
+        # Other dtypes or shapes: pack to f32 (and validate) first.
+        proj, params, perm = _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm)
+        args = (params.data_ptr(), params.data_ptr() + 4, params.data_ptr() + 8,
+                params.data_ptr() + 12, 0, perm.data_ptr(), 0)
+    else:
+        # The parameters as they are: the kernel reads them in their own dtype.
+        proj = _bf16("proj", proj)
+        a_pre, a_post, a_res = (a.contiguous() for a in (alpha_pre, alpha_post, alpha_res))
+        bias, perm = bias.contiguous(), perm.contiguous()
+        args = (a_pre.data_ptr(), a_post.data_ptr(), a_res.data_ptr(), bias.data_ptr(), pdt,
+                perm.data_ptr(), qdt)
     T = proj.shape[0]
     f = dict(device=proj.device, dtype=torch.float32)
     h_pre, h_post, H = torch.empty((T, 4), **f), torch.empty((T, 4), **f), torch.empty((T, 4, 4), **f)
     with _on_device(proj):
-        _native.call("fmhc_k2_fwd", proj.data_ptr(), params.data_ptr(), perm.data_ptr(),
-                     h_pre.data_ptr(), h_post.data_ptr(), H.data_ptr(), T, _stream(proj))
+        _native.call("fmhc_k2_fwd_typed", proj.data_ptr(), *args, h_pre.data_ptr(),
+                     h_post.data_ptr(), H.data_ptr(), T, _stream(proj))
     return h_pre, h_post, H
 
 

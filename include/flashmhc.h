@@ -230,6 +230,23 @@ FMHC_API int fmhc_k2_fwd(const void *proj, const float *params, const float *per
                          float *h_pre, float *h_post, float *H_merged, int64_t T,
                          void *stream);
 
+/* Element types of fmhc_k2_fwd_typed's parameter pointers. */
+enum fmhc_dtype { FMHC_DTYPE_F32 = 0, FMHC_DTYPE_BF16 = 1 };
+
+/* ------------------------------------------------------------------------
+ * The same K2 forward reading the parameters where they live, in their own
+ * dtype (f32 or bf16, `param_dtype` for the three alphas and the 32 bias
+ * entries, `perm_dtype` for perm (24, 16)): a module's alpha_pre, alpha_post,
+ * alpha_res, W_all.bias and perm_mat tensors are passed as they are, so no
+ * packing launch runs before it and a captured CUDA graph reads the live
+ * values.  Results are identical to fmhc_k2_fwd on the packed f32 copy.
+ * No counterpart in the reference (see fmhc_k2_fwd).
+ */
+FMHC_API int fmhc_k2_fwd_typed(const void *proj, const void *alpha_pre, const void *alpha_post,
+                               const void *alpha_res, const void *bias, int param_dtype,
+                               const void *perm, int perm_dtype, float *h_pre, float *h_post,
+                               float *H_merged, int64_t T, void *stream);
+
 /* ------------------------------------------------------------------------
  * K2 backward: given the f32 gradients of h_pre, h_post and H_merged, returns
  * grad_proj (T, 32) bf16 and grad_params (35,) f32 (summed over tokens in a

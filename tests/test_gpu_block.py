@@ -153,9 +153,11 @@ def test_eval_no_grad_tiny_T_with_outliers(T):
     x[:, :, rng.choice(C, size=C // 100, replace=False)] *= 100.0
     xb = torch.from_numpy(x).cuda().to(torch.bfloat16)
     with torch.no_grad():
-        out = blk(xb)
+        out = blk(xb)  # the no-grad fast path (no autograd Functions, no op dispatch)
         ref = blk._forward_pytorch(xb)
     assert out.shape == (T, 4, C)
+    # Same kernels as the grad-enabled path, so the same bits.
+    assert torch.equal(blk(xb).detach(), out)
     # Both paths round the coefficients to bf16 but at different points (the
     # fused K2 keeps f32 intermediates), so they may differ by one bf16 step of
     # a coefficient, multiplied by |x| (x100 in the outlier channels) and by

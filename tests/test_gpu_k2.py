@@ -103,3 +103,38 @@ def test_k2_autograd_through_block_params():
     assert torch.equal(proj.grad, g_proj)
     assert torch.equal(blk.W_all.bias.grad, gp[3:])
     assert torch.equal(blk.alpha_res.grad, gp[2:3])
+
+
+@pytest.mark.parametrize("param_dtype", [torch.float32, torch.bfloat16])
+def test_k2_typed_entry_matches_packed_entry(param_dtype):
+    """fmhc_k2_fwd_typed (parameters read where they live, f32 or bf16) gives
+    the same bits as fmhc_k2_fwd on the packed f32 copy of the parameters."""
+    from flash_mhc import _native
+
+    blk, proj = _setup(1000, 11)
+    blk = blk.to(param_dtype)
+    a = [blk.alpha_pre, blk.alpha_post, blk.alpha_res]
+    packed = torch.cat([t.reshape(-1) for t in a] + [blk.W_all.bias.reshape(-1)]).float().contiguous()
+    perm32 = blk.perm_mat.float().contiguous()
+    T = proj.shape[0]
+    outs = []
+    for typed in (False, True):
+        hp = torch.empty(T, 4, device="cuda")
+        hq = torch.empty(T, 4, device="cuda")
+        H = torch.empty(T, 4, 4, device="cuda")
+        st = torch.cuda.current_stream().cuda_stream
+        if typed:
+            dt = 1 if param_dtype == torch.bfloat16 else 0
+            _native.call("fmhc_k2_fwd_typed", proj.data_ptr(), a[0].data_ptr(), a[1].data_ptr(),
+                         a[2].data_ptr(), blk.W_all.bias.data_ptr(), dt, blk.perm_mat.data_ptr(), dt,
+                         hp.data_ptr(), hq.data_ptr(), H.data_ptr(), T, st)
+        else:
+            _native.call("fmhc_k2_fwd", proj.data_ptr(), packed.data_ptr(), perm32.data_ptr(),
+                         hp.data_ptr(), hq.data_ptr(), H.data_ptr(), T, st)
+        outs.append((hp, hq, H))
+    for x, y in zip(*outs):
+        assert torch.equal(x, y)
+    # and the op (which takes the typed entry for f32/bf16 parameters)
+    got = torch.ops.flash_mhc.mhc_coeffs(proj, *a, blk.W_all.bias, blk.perm_mat)
+    for x, y in zip(got, outs[0]):
+        assert torch.equal(x, y)
