@@ -281,6 +281,234 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   }
 }
 
+// ---------------------------------------------------------------------------
+// K1 forward, split-K over a thread-block cluster (a few thousand tokens).
+//
+// With few token tiles, each CTA of the persistent kernel above walks all
+// nC / 64 k-steps of a small tile one after another and the launch is
+// latency-bound (~29 us at T = 8192, nC = 4096).  Here a cluster of S CTAs
+// (S = 2 or 4) takes one 128-row tile; CTA r of the cluster runs the k-steps
+// [r nk / S, (r + 1) nk / S) with the same pipeline (TMA producer, tcgen05
+// MMA into TMEM, row warps taking the sum of squares from the stages).  The S
+// partials of each row (32 projections and the sum of squares) are then added
+// up a binary tree through distributed shared memory, in a fixed order:
+// round 1, rank r + 1 -> rank r for even r; round 2 (S = 4), rank 2 -> rank 0,
+// so rank 0 holds (p0 + p1) + (p2 + p3).  A sender's row threads store their
+// 33 values into the receiver's buffer for that round and arrive (release,
+// cluster scope) on the receiver's mbarrier; the receiver waits (bounded,
+// acquire) and adds.  Senders then exit: no CTA reads another's buffer after
+// its owner may have left.  Rank 0 finishes: inv_rms = rsqrt(ss / nC + eps),
+// out = bf16(proj * inv_rms).  Nothing here addresses another GPU.
+constexpr int kSkStages = 3;
+constexpr int kSkRows = 128;
+struct alignas(1024) SkSmem {
+  uint8_t stage[kSkStages][kStageBytes];
+  float recv[2][kSkRows][33];  // partials received in rounds 1 and 2
+  uint64_t full[kSkStages];
+  uint64_t empty[kSkStages];
+  uint64_t tfull;
+  uint64_t rfull[2];           // 128 remote arrivals (one per sender row thread)
+  uint64_t mma_done;
+  uint32_t tmem_base;
+  int abort;
+};
+
+enum : unsigned { kSiteSkProdEmpty = 0x111, kSiteSkMmaFull = 0x112, kSiteSkRowFull = 0x113,
+                  kSiteSkTfull = 0x114, kSiteSkRecv = 0x115, kSiteSkDrain = 0x116 };
+
+__device__ __forceinline__ void sk_send(SkSmem &sm, const float (&acc)[33], int r, int slot,
+                                        uint32_t dst) {
+  const uint32_t base = mapa_shared(smem_u32(&sm.recv[slot][r][0]), dst);
+#pragma unroll
+  for (int j = 0; j < 33; ++j) st_cluster_f32(base + 4 * j, acc[j]);
+  mbar_arrive_remote(mapa_shared(smem_u32(&sm.rfull[slot]), dst));
+}
+
+__global__ void __launch_bounds__(kThreads, FMHC_K1F_CTAS_PER_SM)
+k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
+                        const __grid_constant__ CUtensorMap tmap_w,
+                        __nv_bfloat16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T,
+                        int nC, int S) {
+  extern __shared__ uint8_t smem_raw[];
+  SkSmem &sm = *reinterpret_cast<SkSmem *>(
+      (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  volatile int *abort = &sm.abort;
+  const uint32_t rank = cluster_ctarank();
+  const int64_t row0 = int64_t(blockIdx.x / S) * kSkRows;
+  const int64_t rows = (T - row0) < kSkRows ? (T - row0) : kSkRows;
+  const int nbox = int((rows + kBoxRows - 1) / kBoxRows);
+  const int nk = nC / kBK;
+  const int kb0 = int(rank) * nk / S, kb1 = (int(rank) + 1) * nk / S;
+
+  if (threadIdx.x == 0) {
+    for (int st = 0; st < kSkStages; ++st) {
+      mbar_init(smem_u32(&sm.full[st]), 1);
+      mbar_init(smem_u32(&sm.empty[st]), 1 + kRowThreads);
+    }
+    mbar_init(smem_u32(&sm.tfull), 1);
+    mbar_init(smem_u32(&sm.rfull[0]), kRowThreads);
+    mbar_init(smem_u32(&sm.rfull[1]), kRowThreads);
+    mbar_init(smem_u32(&sm.mma_done), 1);
+    sm.abort = 0;
+    fence_mbar_init();
+    prefetch_tmap(&tmap_x);
+    prefetch_tmap(&tmap_w);
+  }
+  if (warp == 1) {
+    tmem_alloc(smem_u32(&sm.tmem_base), 32);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  // Every CTA's barriers exist before any peer arrives on them.
+  cluster_sync_all();
+  const uint32_t tmem = sm.tmem_base;
+  // No global memory is touched before this point (see pdl_wait()).
+  pdl_wait();
+
+  if (warp == 0) {
+    // ---------------------------------------------------------- producer
+    if (lane == 0) {
+      int stage = 0, issued = 0;
+      uint32_t phase = 0;
+      for (int kb = kb0; kb < kb1 && !*abort; ++kb) {
+        if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, abort, kSiteSkProdEmpty)) break;
+        const uint32_t full = smem_u32(&sm.full[stage]);
+        mbar_arrive_expect_tx(full, uint32_t(kColBoxes * (nbox * kBoxBytes + kColBBytes)));
+        const uint32_t a = smem_u32(sm.stage[stage]);
+        for (int cb = 0; cb < kColBoxes; ++cb) {
+          const int32_t k0 = kb * kBK + cb * 64;
+          for (int b = 0; b < nbox; ++b)
+            tma_load_2d(a + cb * kColABytes + b * kBoxBytes, &tmap_x, full, k0,
+                        int32_t(row0 + b * kBoxRows));
+          tma_load_2d(a + kABytes + cb * kColBBytes, &tmap_w, full, k0, 0);
+        }
+        ++issued;
+        if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+      }
+      int n = issued < kSkStages ? issued : kSkStages;
+      int st = stage;
+      uint32_t ph = phase;
+      for (int i = 0; i < n; ++i) {
+        if (--st < 0) { st = kSkStages - 1; ph ^= 1; }
+        mbar_wait(smem_u32(&sm.full[st]), ph, abort, kSiteSkDrain, true);
+      }
+    }
+  } else if (warp == 1) {
+    // -------------------------------------------------------- MMA issuer
+    if (lane == 0) {
+      constexpr uint32_t idesc = idesc_bf16_f32(kBM, kND, 0, 0);
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int kb = kb0; kb < kb1; ++kb) {
+        if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteSkMmaFull)) { ok = false; break; }
+        tc_fence_after();
+        const uint32_t a = smem_u32(sm.stage[stage]);
+#pragma unroll
+        for (int k = 0; k < kBK / 16; ++k) {
+          const int cb = k / 4, kk = k % 4;
+          const uint64_t ad = smem_desc(a + cb * kColABytes + kk * 32, 16, 1024, 2);
+          const uint64_t bd = smem_desc(a + kABytes + cb * kColBBytes + kk * 32, 16, 1024, 2);
+          mma_bf16_ss(tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
+        }
+        mma_commit(smem_u32(&sm.empty[stage]));
+        if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+      }
+      if (ok) mma_commit(smem_u32(&sm.tfull));
+      mma_commit(smem_u32(&sm.mma_done));
+      mbar_wait(smem_u32(&sm.mma_done), 0, abort, kSiteSkDrain, true);
+    }
+  } else {
+    // ---------------------------------- row warps: sumsq, partial, tree
+    const int q = warp & 3;
+    const int r = q * 32 + lane;
+    int stage = 0;
+    uint32_t phase = 0;
+    float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+    bool ok = true;
+    for (int kb = kb0; kb < kb1; ++kb) {
+      if (!mbar_wait(smem_u32(&sm.full[stage]), phase, abort, kSiteSkRowFull)) { ok = false; break; }
+#pragma unroll
+      for (int cb = 0; cb < kColBoxes; ++cb) {
+        const uint8_t *row = sm.stage[stage] + cb * kColABytes + r * 128;
+        uint4 u[8];
+#pragma unroll
+        for (int i = 0; i < 8; ++i) u[i] = *reinterpret_cast<const uint4 *>(row + (((i + r) & 7) << 4));
+#pragma unroll
+        for (int i = 0; i < 8; ++i) {
+          float f;
+          f = bf16lo(u[i].x); ss8[0] = fmaf(f, f, ss8[0]); f = bf16hi(u[i].x); ss8[1] = fmaf(f, f, ss8[1]);
+          f = bf16lo(u[i].y); ss8[2] = fmaf(f, f, ss8[2]); f = bf16hi(u[i].y); ss8[3] = fmaf(f, f, ss8[3]);
+          f = bf16lo(u[i].z); ss8[4] = fmaf(f, f, ss8[4]); f = bf16hi(u[i].z); ss8[5] = fmaf(f, f, ss8[5]);
+          f = bf16lo(u[i].w); ss8[6] = fmaf(f, f, ss8[6]); f = bf16hi(u[i].w); ss8[7] = fmaf(f, f, ss8[7]);
+        }
+      }
+      fence_proxy_async_smem();
+      mbar_arrive(smem_u32(&sm.empty[stage]));
+      if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+    }
+    if (ok && mbar_wait(smem_u32(&sm.tfull), 0, abort, kSiteSkTfull)) {
+      tc_fence_after();
+      uint32_t v[32];
+      tmem_ld_32x32b_x32(tmem + (uint32_t(q * 32) << 16), v);
+      tmem_wait_ld();
+      float acc[33];
+#pragma unroll
+      for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
+      acc[32] = ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
+      bool done = false;
+      // Round 1: odd ranks send to rank - 1.
+      if (rank & 1u) {
+        sk_send(sm, acc, r, 0, rank - 1);
+        done = true;
+      } else if (mbar_wait_cluster(smem_u32(&sm.rfull[0]), 0, abort, kSiteSkRecv)) {
+#pragma unroll
+        for (int j = 0; j < 33; ++j) acc[j] += sm.recv[0][r][j];
+      } else {
+        done = true;
+      }
+      // Round 2 (S = 4): rank 2 sends to rank 0.
+      if (!done && S == 4) {
+        if (rank == 2) {
+          sk_send(sm, acc, r, 1, 0);
+          done = true;
+        } else if (mbar_wait_cluster(smem_u32(&sm.rfull[1]), 0, abort, kSiteSkRecv)) {
+#pragma unroll
+          for (int j = 0; j < 33; ++j) acc[j] += sm.recv[1][r][j];
+        } else {
+          done = true;
+        }
+      }
+      if (!done && rank == 0 && r < rows) {
+        const int64_t t = row0 + r;
+        const float inv = rsqrtf(acc[32] / float(nC) + kEps);
+        uint4 *o = reinterpret_cast<uint4 *>(out + t * kND);
+#pragma unroll
+        for (int c = 0; c < 4; ++c) {
+          uint4 w;
+          w.x = pack_bf16x2(acc[8 * c + 0] * inv, acc[8 * c + 1] * inv);
+          w.y = pack_bf16x2(acc[8 * c + 2] * inv, acc[8 * c + 3] * inv);
+          w.z = pack_bf16x2(acc[8 * c + 4] * inv, acc[8 * c + 5] * inv);
+          w.w = pack_bf16x2(acc[8 * c + 6] * inv, acc[8 * c + 7] * inv);
+          __stcs(o + c, w);
+        }
+        __stcs(inv_rms + t, inv);
+      }
+    }
+  }
+
+  tc_fence_before();
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, 32);
+  }
+}
+
 }  // namespace k1tc
 }  // namespace fmhc
 
@@ -376,6 +604,8 @@ const char *k1_tc_error() { return k1tc::g_msg; }
 static_assert(sizeof(k1tc::BwdSmem) + 1024 <= 232448, "K1 backward shared memory");
 static_assert((sizeof(k1tc::FwdSmem) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
               "K1 forward shared memory");
+static_assert((sizeof(k1tc::SkSmem) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
+              "split-K K1 forward shared memory");
 
 bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
                          int64_t T, int64_t nC, int64_t D) {
@@ -389,6 +619,44 @@ bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const fl
 int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t T, int nC,
                      cudaStream_t s) {
   using namespace k1tc;
+  // Few 128-row tiles: split k over clusters of S CTAs.  Measured (profiler
+  // kernel times, nC = 4096; nC = 3072 alike): S = 4 while the clusters fit
+  // one CTA per SM (T <= 4736: 24 -> 18.6 us at T = 1024..4096); S = 2 while
+  // they fill at most 3/4 of the two-CTA-per-SM slots (T <= 14208: 31.5 ->
+  // 22.0 us at T = 8192; S = 4 there, two CTAs per SM, 28.1 us); beyond that
+  // the persistent kernel (S = 2 at T = 16384: 34.1 against 33.6 us).
+  {
+    const int64_t tiles = (T + kSkRows - 1) / kSkRows;
+    const int64_t sms = device_sms();
+    const int64_t slots = sms * FMHC_K1F_CTAS_PER_SM;
+    const int nk = nC / kBK;
+    int S = 0;
+#ifndef FMHC_K1F_SPLITK  // 0 disables the split-K path (A/B measurements)
+#define FMHC_K1F_SPLITK 1
+#endif
+    if (FMHC_K1F_SPLITK && tiles * 4 <= sms && nk >= 8) S = 4;
+    else if (FMHC_K1F_SPLITK && tiles * 2 * 4 <= slots * 3 && nk >= 4) S = 2;
+    if (S) {
+      CUtensorMap mx, mw;
+      if (!make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBoxRows,
+                    CU_TENSOR_MAP_SWIZZLE_128B) ||
+          !make_map(&mw, W, uint64_t(nC), kND, uint64_t(nC) * 2, 64, kND,
+                    CU_TENSOR_MAP_SWIZZLE_128B)) {
+        snprintf(g_msg, sizeof(g_msg), "cuTensorMapEncodeTiled failed");
+        return 5;
+      }
+      const size_t smem = sizeof(SkSmem) + 1024;
+      if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_splitk_kernel), smem))
+        return e;
+      if (launch_cluster(k1_fwd_tc_splitk_kernel, dim3(unsigned(tiles * S)), dim3(kThreads), smem,
+                         s, unsigned(S), mx, mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms,
+                         T, nC, S) != cudaSuccess) {
+        snprintf(g_msg, sizeof(g_msg), "cluster launch of the split-K K1 forward failed");
+        return 4;
+      }
+      return 0;
+    }
+  }
   CUtensorMap mx, mw;
   if (!make_map(&mx, x, uint64_t(nC), uint64_t(T), uint64_t(nC) * 2, 64, kBoxRows,
                 CU_TENSOR_MAP_SWIZZLE_128B) ||
