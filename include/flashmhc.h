@@ -116,8 +116,10 @@ FMHC_API int fmhc_k1_bwd(const void *grad_out, const void *x, const void *W,
  * memory pool), serving runtimes that reserve all HBM up front, and
  * latency-critical paths where cudaMalloc (which can synchronise the device)
  * is not allowed.
- * Limit: fmhc_k1_bwd_workspace_size(T, nC, D) must not exceed 32 MiB (this
- * covers, e.g., T = 131072 tokens at nC = 16384); larger calls fail with
+ * Limit: fmhc_k1_bwd_workspace_size(T, nC, D) must not exceed 32 MiB.  On
+ * the tensor-core path (nC a multiple of 128) the workspace is the grad_W
+ * partials alone, at most 18.5 MiB at any T; the CUDA-core path needs up to
+ * 2 KiB x nC, so it fits up to nC = 16384.  Larger calls fail with
  * FMHC_ERR_WORKSPACE and should use fmhc_k1_bwd.  Every GPU that loads the
  * library holds the 32 MiB until the process exits.  The first call on each
  * device looks up the array's device address; make it before any stream
