@@ -53,13 +53,14 @@ using bf16 = __nv_bfloat16;
 template <int VEC, int U, int MINB>
 __global__ void __launch_bounds__(256, MINB)
 k3_fwd_kernel(const bf16 *__restrict__ x, const float4 *__restrict__ hp,
-              bf16 *__restrict__ out, int64_t T, int C) {
+              bf16 *__restrict__ out, int64_t T, int C, int rev) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int nchunk = C / VEC;
-  for (int64_t t = warp; t < T; t += nwarps) {
+  for (int64_t i = warp; i < T; i += nwarps) {
+    const int64_t t = rev ? T - 1 - i : i;  // sweep direction (sweep_dir())
     const float4 h = __ldg(hp + t);
     const bf16 *xr = x + t * 4 * C;
     bf16 *orow = out + t * C;
@@ -98,13 +99,14 @@ template <int VEC, int U, int MINB>
 __global__ void __launch_bounds__(256, MINB)
 k3_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const float4 *__restrict__ hp, bf16 *__restrict__ gx,
-              float *__restrict__ gh, int64_t T, int C) {
+              float *__restrict__ gh, int64_t T, int C, int rev) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int nchunk = C / VEC;
-  for (int64_t t = warp; t < T; t += nwarps) {
+  for (int64_t i = warp; i < T; i += nwarps) {
+    const int64_t t = rev ? T - 1 - i : i;  // sweep direction (sweep_dir())
     const float4 h = __ldg(hp + t);
     const float hj[4] = {h.x, h.y, h.z, h.w};
     const bf16 *xr = x + t * 4 * C;
@@ -152,13 +154,14 @@ template <int VEC, int U, int MINB>
 __global__ void __launch_bounds__(256, MINB)
 k4_fwd_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ lo,
               const float4 *__restrict__ H, const float4 *__restrict__ hpost,
-              bf16 *__restrict__ out, int64_t T, int C) {
+              bf16 *__restrict__ out, int64_t T, int C, int rev) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int nchunk = C / VEC;
-  for (int64_t t = warp; t < T; t += nwarps) {
+  for (int64_t i = warp; i < T; i += nwarps) {
+    const int64_t t = rev ? T - 1 - i : i;  // sweep direction (sweep_dir())
     float Hm[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -218,13 +221,14 @@ k4_bwd_kernel(const bf16 *__restrict__ go, const bf16 *__restrict__ x,
               const bf16 *__restrict__ lo, const float4 *__restrict__ H,
               const float4 *__restrict__ hpost, bf16 *__restrict__ gx,
               bf16 *__restrict__ glo, float *__restrict__ gH,
-              float *__restrict__ ghp, int64_t T, int C) {
+              float *__restrict__ ghp, int64_t T, int C, int rev) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int nchunk = C / VEC;
-  for (int64_t t = warp; t < T; t += nwarps) {
+  for (int64_t i = warp; i < T; i += nwarps) {
+    const int64_t t = rev ? T - 1 - i : i;  // sweep direction (sweep_dir())
     float Hm[4][4];
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
@@ -318,13 +322,14 @@ template <int VEC, int U, int MODE>
 __global__ void __launch_bounds__(256)
 grad_x_combine_kernel(const bf16 *__restrict__ gx1, const bf16 *__restrict__ gli,
                       const float4 *__restrict__ hp, const bf16 *__restrict__ k4,
-                      const float4 *__restrict__ H, bf16 *__restrict__ gx, int64_t T, int C) {
+                      const float4 *__restrict__ H, bf16 *__restrict__ gx, int64_t T, int C, int rev) {
   pdl_wait();
   const int lane = threadIdx.x & 31;
   const int64_t warp = (int64_t(blockIdx.x) * blockDim.x + threadIdx.x) >> 5;
   const int64_t nwarps = (int64_t(gridDim.x) * blockDim.x) >> 5;
   const int nchunk = C / VEC;
-  for (int64_t t = warp; t < T; t += nwarps) {
+  for (int64_t i = warp; i < T; i += nwarps) {
+    const int64_t t = rev ? T - 1 - i : i;  // sweep direction (sweep_dir())
     const float4 h = __ldg(hp + t);
     const float hj[4] = {h.x, h.y, h.z, h.w};
     float Hm[4][4];
@@ -430,6 +435,26 @@ int grid_for(K kernel, int64_t T, int threads) {
 namespace {
 constexpr int kThreads = 256;
 
+// Token sweep direction of each streaming kernel.  Every kernel of the path
+// reads x (T, 4, C), and at its end the L2 holds the tokens it touched last;
+// the next kernel starting from that end reads them from L2 instead of HBM.
+// The grid-stride loops sweep all tokens coherently (warp w handles the w-th
+// token of the current window), so alternating directions between
+// consecutive kernels of the step K1f, K3f, K4f, K4b, K3b, K1b gives every
+// boundary that reuse: K3f forward, K4f backward, K4b forward, K3b backward
+// (K1b sweeps forward; K1f gives each CTA a contiguous range, so it has no
+// single direction).  In the block's backward the grad_x combination follows
+// K1b and reads K1b's grad_x backward, from its most recently written end.
+// Outputs are per token, so the direction changes no result bit.
+#ifndef FMHC_SWEEP_ALT  // 0: every kernel sweeps forward (A/B measurements)
+#define FMHC_SWEEP_ALT 1
+#endif
+enum SweepKernel { kK3Fwd, kK4Fwd, kK4Bwd, kK3Bwd, kCombine };
+inline int sweep_dir(SweepKernel k) {
+  if (!FMHC_SWEEP_ALT) return 0;
+  return (k == kK4Fwd || k == kK3Bwd || k == kCombine) ? 1 : 0;
+}
+
 }  // namespace
 
 #define FMHC_DISPATCH_VEC(VEC_RT, ...)                      \
@@ -445,7 +470,7 @@ void launch_k3_fwd(const void *x, const float *hp, void *out, int64_t T, int C, 
   FMHC_DISPATCH_VEC(vec, {
     auto k = k3_fwd_kernel<VEC, FMHC_K3F_U, FMHC_K3F_MINB>;
     launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)x,
-           (const float4 *)hp, (bf16 *)out, T, C);
+           (const float4 *)hp, (bf16 *)out, T, C, sweep_dir(kK3Fwd));
   });
 }
 
@@ -454,7 +479,7 @@ void launch_k3_bwd(const void *go, const void *x, const float *hp, void *gx, flo
   FMHC_DISPATCH_VEC(vec, {
     auto k = k3_bwd_kernel<VEC, FMHC_K3B_U, FMHC_K3B_MINB>;
     launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
-           (const bf16 *)x, (const float4 *)hp, (bf16 *)gx, gh, T, C);
+           (const bf16 *)x, (const float4 *)hp, (bf16 *)gx, gh, T, C, sweep_dir(kK3Bwd));
   });
 }
 
@@ -463,7 +488,7 @@ void launch_k4_fwd(const void *x, const void *lo, const float *H, const float *h
   FMHC_DISPATCH_VEC(vec, {
     auto k = k4_fwd_kernel<VEC, FMHC_K4F_U, FMHC_K4F_MINB>;
     launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)x,
-           (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)out, T, C);
+           (const bf16 *)lo, (const float4 *)H, (const float4 *)hp, (bf16 *)out, T, C, sweep_dir(kK4Fwd));
   });
 }
 
@@ -474,12 +499,12 @@ void launch_grad_x_combine(const void *gx1, const void *gli, const float *hp, co
       auto k = grad_x_combine_kernel<VEC, 2, 1>;
       launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
              (const bf16 *)gli, (const float4 *)hp, (const bf16 *)gx4, (const float4 *)nullptr,
-             (bf16 *)gx, T, C);
+             (bf16 *)gx, T, C, sweep_dir(kCombine));
     } else {
       auto k = grad_x_combine_kernel<VEC, 2, 0>;
       launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
              (const bf16 *)gli, (const float4 *)hp, (const bf16 *)nullptr, (const float4 *)nullptr,
-             (bf16 *)gx, T, C);
+             (bf16 *)gx, T, C, sweep_dir(kCombine));
     }
   });
 }
@@ -491,7 +516,7 @@ void launch_grad_x_combine_post(const void *gx1, const void *gli, const float *h
     auto k = grad_x_combine_kernel<VEC, 2, 2>;
     launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)gx1,
            (const bf16 *)gli, (const float4 *)hp, (const bf16 *)go, (const float4 *)H,
-           (bf16 *)gx, T, C);
+           (bf16 *)gx, T, C, sweep_dir(kCombine));
   });
 }
 
@@ -503,12 +528,12 @@ void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H
       auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB, true>;
       launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
              (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp,
-             (bf16 *)gx, (bf16 *)glo, gH, ghp, T, C);
+             (bf16 *)gx, (bf16 *)glo, gH, ghp, T, C, sweep_dir(kK4Bwd));
     } else {
       auto k = k4_bwd_kernel<VEC, FMHC_K4B_U, FMHC_K4B_MINB, false>;
       launch(k, dim3(grid_for(k, T, kThreads)), dim3(kThreads), 0, s, (const bf16 *)go,
              (const bf16 *)x, (const bf16 *)lo, (const float4 *)H, (const float4 *)hp,
-             (bf16 *)nullptr, (bf16 *)glo, gH, ghp, T, C);
+             (bf16 *)nullptr, (bf16 *)glo, gH, ghp, T, C, sweep_dir(kK4Bwd));
     }
   });
 }
