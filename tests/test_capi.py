@@ -61,6 +61,14 @@ def test_argument_validation_without_gpu():
     ws = ctypes.c_void_p(4096)
     st, msg = _status("fmhc_k1_bwd", p, p, p, p, p, p, p, ws, 0, 8, 256, 32, None)
     assert st == 6 and "workspace" in msg
+    st, msg = _status("fmhc_k2_fwd_typed", p, p, p, p, p, 7, p, 0, p, p, p, 8, None)
+    assert st == 2 and "dtype" in msg
+    st, msg = _status("fmhc_mhc_grad_x_combine_post", p, p, p, p, p, p, 8, 3, 64, None)
+    assert st == 1 and "n=4" in msg
+    # K4 backward accepts grad_x = NULL (parameter gradients only); the other
+    # outputs are still required
+    st, msg = _status("fmhc_k4_bwd", p, p, p, p, p, None, None, p, p, 8, 4, 64, None)
+    assert st == 1 and "NULL" in msg
     # T == 0 is a no-op that succeeds without touching the device
     st, msg = _status("fmhc_k4_bwd", None, None, None, None, None, None, None, None, None,
                       0, 4, 64, None)
