@@ -292,9 +292,9 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 // MMA into TMEM, row warps taking the sum of squares from the stages).  The S
 // partials of each row (32 projections and the sum of squares) are then added
 // up a binary tree through distributed shared memory, in a fixed order:
-// round 1, rank r + 1 -> rank r for even r; round 2 (S = 4), rank 2 -> rank 0,
+// first level, rank r + 1 -> rank r for even r; second level (S = 4), rank 2 -> rank 0,
 // so rank 0 holds (p0 + p1) + (p2 + p3).  A sender's row threads store their
-// 33 values into the receiver's buffer for that round and arrive (release,
+// 33 values into the receiver's buffer for that level and arrive (release,
 // cluster scope) on the receiver's mbarrier; the receiver waits (bounded,
 // acquire) and adds.  Senders then exit: no CTA reads another's buffer after
 // its owner may have left.  Rank 0 finishes: inv_rms = rsqrt(ss / nC + eps),
@@ -303,7 +303,7 @@ constexpr int kSkStages = 3;
 constexpr int kSkRows = 128;
 struct alignas(1024) SkSmem {
   uint8_t stage[kSkStages][kStageBytes];
-  float recv[2][kSkRows][33];  // partials received in rounds 1 and 2
+  float recv[2][kSkRows][33];  // partials received at the first and second level
   uint64_t full[kSkStages];
   uint64_t empty[kSkStages];
   uint64_t tfull;
@@ -461,7 +461,7 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
       for (int j = 0; j < 32; ++j) acc[j] = __uint_as_float(v[j]);
       acc[32] = ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
       bool done = false;
-      // Round 1: odd ranks send to rank - 1.
+      // First level: odd ranks send to rank - 1.
       if (rank & 1u) {
         sk_send(sm, acc, r, 0, rank - 1);
         done = true;
@@ -471,7 +471,7 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
       } else {
         done = true;
       }
-      // Round 2 (S = 4): rank 2 sends to rank 0.
+      // Second level (S = 4): rank 2 sends to rank 0.
       if (!done && S == 4) {
         if (rank == 2) {
           sk_send(sm, acc, r, 1, 0);
