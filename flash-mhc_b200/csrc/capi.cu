@@ -355,8 +355,58 @@ int fmhc_k2_bwd(const void *proj, const float *params, const float *perm, const 
   if (workspace_bytes < need)
     return fail(FMHC_ERR_WORKSPACE, "%s: workspace of %lld bytes, %lld needed", w,
                 (long long)workspace_bytes, (long long)need);
-  fmhc::launch_k2_bwd(proj, params, perm, grad_h_pre, grad_h_post, grad_H_merged, grad_proj,
-                      grad_params, (float *)workspace, T, s);
+  fmhc::launch_k2_bwd(proj, fmhc::k2_packed_params(params, perm), grad_h_pre, grad_h_post,
+                      grad_H_merged, grad_proj, fmhc::k2_packed_grads(grad_params),
+                      (float *)workspace, T, s);
+  return check_launch(w);
+}
+
+int fmhc_k2_bwd_typed(const void *proj, const void *alpha_pre, const void *alpha_post,
+                      const void *alpha_res, const void *bias, int param_dtype, const void *perm,
+                      int perm_dtype, const float *grad_h_pre, const float *grad_h_post,
+                      const float *grad_H_merged, void *grad_proj, void *grad_alpha_pre,
+                      void *grad_alpha_post, void *grad_alpha_res, void *grad_bias,
+                      void *workspace, int64_t workspace_bytes, int64_t T, void *stream) {
+  const char *w = "fmhc_k2_bwd_typed";
+  if (T < 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: T must be >= 0 (got %lld)", w, (long long)T);
+  const auto dt_ok = [](int d) { return d == FMHC_DTYPE_F32 || d == FMHC_DTYPE_BF16; };
+  if (!dt_ok(param_dtype) || !dt_ok(perm_dtype))
+    return fail(FMHC_ERR_UNSUPPORTED, "%s: parameter dtypes must be FMHC_DTYPE_F32 or FMHC_DTYPE_BF16", w);
+  FMHC_REQUIRE_PTR(w, grad_alpha_pre); FMHC_REQUIRE_PTR(w, grad_alpha_post);
+  FMHC_REQUIRE_PTR(w, grad_alpha_res); FMHC_REQUIRE_PTR(w, grad_bias);
+  const uintptr_t pa = param_dtype == FMHC_DTYPE_BF16 ? 2 : 4;
+  const uintptr_t qa = perm_dtype == FMHC_DTYPE_BF16 ? 2 : 4;
+  if (!aligned(grad_alpha_pre, pa) || !aligned(grad_alpha_post, pa) ||
+      !aligned(grad_alpha_res, pa) || !aligned(grad_bias, pa))
+    return fail(FMHC_ERR_ALIGNMENT, "%s: parameter gradients must be aligned to their element size", w);
+  const fmhc::K2ParamGrads G{grad_alpha_pre, grad_alpha_post, grad_alpha_res, grad_bias,
+                             param_dtype == FMHC_DTYPE_BF16 ? 1 : 0};
+  cudaStream_t s = (cudaStream_t)stream;
+  if (T == 0) {
+    fmhc::launch_k2_bwd(nullptr, fmhc::K2Params{}, nullptr, nullptr, nullptr, nullptr, G, nullptr,
+                        0, s);
+    return check_launch(w);
+  }
+  FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, alpha_pre); FMHC_REQUIRE_PTR(w, alpha_post);
+  FMHC_REQUIRE_PTR(w, alpha_res); FMHC_REQUIRE_PTR(w, bias); FMHC_REQUIRE_PTR(w, perm);
+  FMHC_REQUIRE_PTR(w, grad_h_pre); FMHC_REQUIRE_PTR(w, grad_h_post);
+  FMHC_REQUIRE_PTR(w, grad_H_merged); FMHC_REQUIRE_PTR(w, grad_proj); FMHC_REQUIRE_PTR(w, workspace);
+  FMHC_REQUIRE_ALIGN16(w, proj); FMHC_REQUIRE_ALIGN16(w, grad_h_pre);
+  FMHC_REQUIRE_ALIGN16(w, grad_h_post); FMHC_REQUIRE_ALIGN16(w, grad_H_merged);
+  FMHC_REQUIRE_ALIGN16(w, grad_proj);
+  if (!aligned(alpha_pre, pa) || !aligned(alpha_post, pa) || !aligned(alpha_res, pa) ||
+      !aligned(bias, pa) || !aligned(perm, qa))
+    return fail(FMHC_ERR_ALIGNMENT, "%s: parameters must be aligned to their element size", w);
+  if (!aligned(workspace, 256)) return fail(FMHC_ERR_ALIGNMENT, "%s: workspace must be 256-byte aligned", w);
+  const int64_t need = fmhc::k2_bwd_workspace_bytes(T);
+  if (workspace_bytes < need)
+    return fail(FMHC_ERR_WORKSPACE, "%s: workspace of %lld bytes, %lld needed", w,
+                (long long)workspace_bytes, (long long)need);
+  const fmhc::K2Params P{alpha_pre, alpha_post, alpha_res, bias, perm,
+                         param_dtype == FMHC_DTYPE_BF16 ? 1 : 0,
+                         perm_dtype == FMHC_DTYPE_BF16 ? 1 : 0};
+  fmhc::launch_k2_bwd(proj, P, grad_h_pre, grad_h_post, grad_H_merged, grad_proj, G,
+                      (float *)workspace, T, s);
   return check_launch(w);
 }
 

@@ -60,8 +60,16 @@ struct K2Params {
 K2Params k2_packed_params(const float *params, const float *perm);
 void launch_k2_fwd(const void *proj, const K2Params &P, float *h_pre, float *h_post, float *H,
                    int64_t T, cudaStream_t s);
-void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
-                   const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
-                   float *ws, int64_t T, cudaStream_t s);
+// Where K2's backward writes the gradients of a_pre, a_post, a_res (one value
+// each) and bias (32), in f32 (bf16 = 0) or bf16 (bf16 = 1).
+struct K2ParamGrads {
+  void *a_pre, *a_post, *a_res, *bias;
+  int bf16;
+};
+// g_params (35,) f32 = [a_pre, a_post, a_res, bias[32]].
+K2ParamGrads k2_packed_grads(float *g_params);
+void launch_k2_bwd(const void *proj, const K2Params &P, const float *g_hpre, const float *g_hpost,
+                   const float *g_H, void *g_proj, const K2ParamGrads &Gp, float *ws, int64_t T,
+                   cudaStream_t s);
 
 }  // namespace fmhc

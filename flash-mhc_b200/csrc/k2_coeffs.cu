@@ -230,8 +230,9 @@ k2_bwd_kernel(const bf16 *__restrict__ proj, const K2Params P, const float4 *__r
 }
 
 // One warp per parameter: lane l sums blocks l, l+32, ... then a fixed
-// butterfly (deterministic).
-__global__ void k2_param_reduce_kernel(const float *__restrict__ part, float *__restrict__ g_params,
+// butterfly (deterministic).  The sum is written in the parameter's dtype
+// (rounded once from the f32 total when that is bf16).
+__global__ void k2_param_reduce_kernel(const float *__restrict__ part, const K2ParamGrads G,
                                        int nblocks) {
   pdl_wait();
   const int i = blockIdx.x, lane = threadIdx.x;
@@ -239,7 +240,12 @@ __global__ void k2_param_reduce_kernel(const float *__restrict__ part, float *__
   for (int b = lane; b < nblocks; b += 32) s += part[int64_t(b) * kP + i];
 #pragma unroll
   for (int off = 16; off >= 1; off >>= 1) s += __shfl_xor_sync(0xffffffffu, s, off);
-  if (lane == 0) g_params[i] = s;
+  if (lane == 0) {
+    void *dst = i == 0 ? G.a_pre : i == 1 ? G.a_post : i == 2 ? G.a_res : G.bias;
+    const int idx = i < 3 ? 0 : i - 3;
+    if (G.bf16) reinterpret_cast<bf16 *>(dst)[idx] = __float2bfloat16_rn(s);
+    else reinterpret_cast<float *>(dst)[idx] = s;
+  }
 }
 
 int64_t k2_bwd_workspace_bytes(int64_t T) {
@@ -258,14 +264,21 @@ void launch_k2_fwd(const void *proj, const K2Params &P, float *h_pre, float *h_p
          (float4 *)h_post, (float4 *)H, T);
 }
 
-void launch_k2_bwd(const void *proj, const float *params, const float *perm, const float *g_hpre,
-                   const float *g_hpost, const float *g_H, void *g_proj, float *g_params,
-                   float *ws, int64_t T, cudaStream_t s) {
+K2ParamGrads k2_packed_grads(float *g_params) {
+  return K2ParamGrads{g_params, g_params + 1, g_params + 2, g_params + 3, 0};
+}
+
+void launch_k2_bwd(const void *proj, const K2Params &P, const float *g_hpre, const float *g_hpost,
+                   const float *g_H, void *g_proj, const K2ParamGrads &Gp, float *ws, int64_t T,
+                   cudaStream_t s) {
   const unsigned nb = unsigned((T + 255) / 256);
-  launch(k2_bwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj,
-         k2_packed_params(params, perm), (const float4 *)g_hpre, (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj, ws,
+  if (T == 0) {  // empty batch: the parameter gradients are zero
+    launch(k2_param_reduce_kernel, dim3(kP), dim3(32), 0, s, (const float *)nullptr, Gp, 0);
+    return;
+  }
+  launch(k2_bwd_kernel, dim3(nb), dim3(256), 0, s, (const bf16 *)proj, P, (const float4 *)g_hpre, (const float4 *)g_hpost, (const float4 *)g_H, (bf16 *)g_proj, ws,
          T);
-  launch(k2_param_reduce_kernel, dim3(kP), dim3(32), 0, s, ws, g_params, int(nb));
+  launch(k2_param_reduce_kernel, dim3(kP), dim3(32), 0, s, ws, Gp, int(nb));
 }
 
 }  // namespace fmhc

@@ -85,7 +85,7 @@ class _FusedPreMap(torch.autograd.Function):
         if g_li is None:
             g_li = torch.zeros((T, C), device=x.device, dtype=x.dtype)
         g_hpre = ops.pre_map_grad_h(g_li, x, h_pre)
-        g_proj, gp = ops.mhc_coeffs_backward(
+        g_proj, ga_pre, ga_post, ga_res, g_bias = ops.mhc_coeffs_backward_split(
             g_hpre, z(T, 4) if g_hpost is None else g_hpost, z(T, 4, 4) if g_H is None else g_H,
             proj, a_pre, a_post, a_res, bias, perm)
         gx1, gW = ops.fused_rmsnorm_project_backward(g_proj, x.reshape(T, n * C), W, proj, inv)
@@ -95,9 +95,7 @@ class _FusedPreMap(torch.autograd.Function):
             gx = ops.mhc_grad_x_combine(gx1.view(T, n, C), g_li, h_pre, None)
         else:
             gx = ops.mhc_grad_x_combine_post(gx1.view(T, n, C), g_li, h_pre, g_out, H)
-        return (gx, gW, gp[0:1].view_as(a_pre).to(a_pre.dtype),
-                gp[1:2].view_as(a_post).to(a_post.dtype), gp[2:3].view_as(a_res).to(a_res.dtype),
-                gp[3:35].view_as(bias).to(bias.dtype), None, None)
+        return gx, gW, ga_pre, ga_post, ga_res, g_bias, None, None
 
 
 class _FusedPostRes(torch.autograd.Function):

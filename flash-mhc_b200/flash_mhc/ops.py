@@ -68,6 +68,10 @@ _lib.define(
 _lib.define(
     "mhc_coeffs_backward(Tensor grad_h_pre, Tensor grad_h_post, Tensor grad_H_merged, Tensor proj, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor grad_proj, Tensor grad_params)"
 )
+# The same with one gradient per parameter, in the parameter's shape and dtype.
+_lib.define(
+    "mhc_coeffs_backward_split(Tensor grad_h_pre, Tensor grad_h_post, Tensor grad_H_merged, Tensor proj, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor grad_proj, Tensor grad_alpha_pre, Tensor grad_alpha_post, Tensor grad_alpha_res, Tensor grad_bias)"
+)
 
 # ---------------------------------------------------------------------------
 # Autotune controls.  The reference exposes a thread-local context manager and
@@ -134,6 +138,13 @@ def _mhc_coeffs_fake(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
 def _mhc_coeffs_backward_fake(grad_h_pre, grad_h_post, grad_H_merged, proj, alpha_pre,
                               alpha_post, alpha_res, bias, perm):
     return torch.empty_like(proj), torch.empty((35,), device=proj.device, dtype=torch.float32)
+
+
+@torch.library.register_fake("flash_mhc::mhc_coeffs_backward_split")
+def _mhc_coeffs_backward_split_fake(grad_h_pre, grad_h_post, grad_H_merged, proj, alpha_pre,
+                                    alpha_post, alpha_res, bias, perm):
+    return (torch.empty_like(proj), torch.empty_like(alpha_pre), torch.empty_like(alpha_post),
+            torch.empty_like(alpha_res), torch.empty_like(bias))
 
 
 @torch.library.register_fake("flash_mhc::pre_map_grad_h")
@@ -341,6 +352,38 @@ def _mhc_coeffs_backward_cuda(grad_h_pre, grad_h_post, grad_H_merged, proj, alph
     return grad_proj, grad_params
 
 
+@torch.library.impl(_lib, "mhc_coeffs_backward_split", "CUDA")
+def _mhc_coeffs_backward_split_cuda(grad_h_pre, grad_h_post, grad_H_merged, proj, alpha_pre,
+                                    alpha_post, alpha_res, bias, perm):
+    pdt, qdt = _K2_DTYPES.get(bias.dtype), _K2_DTYPES.get(perm.dtype)
+    same = all(a.dtype == bias.dtype for a in (alpha_pre, alpha_post, alpha_res))
+    if pdt is None or qdt is None or not same or proj.dim() != 2 or proj.shape[1] != 32 \
+            or bias.numel() != 32 or perm.shape != (24, 16) \
+            or any(a.numel() != 1 for a in (alpha_pre, alpha_post, alpha_res)):
+        # Other dtypes or shapes: the packed f32 path, then split and cast.
+        g_proj, gp = _mhc_coeffs_backward_cuda(grad_h_pre, grad_h_post, grad_H_merged, proj,
+                                               alpha_pre, alpha_post, alpha_res, bias, perm)
+        return (g_proj, gp[0:1].view_as(alpha_pre).to(alpha_pre.dtype),
+                gp[1:2].view_as(alpha_post).to(alpha_post.dtype),
+                gp[2:3].view_as(alpha_res).to(alpha_res.dtype),
+                gp[3:35].view_as(bias).to(bias.dtype))
+    proj = _bf16("proj", proj)
+    a_pre, a_post, a_res = (a.contiguous() for a in (alpha_pre, alpha_post, alpha_res))
+    bias, perm = bias.contiguous(), perm.contiguous()
+    T = proj.shape[0]
+    g1, g2, g3 = _coef(grad_h_pre), _coef(grad_h_post), _coef(grad_H_merged)
+    grad_proj = torch.empty_like(proj)
+    outs = [torch.empty_like(t) for t in (a_pre, a_post, a_res, bias)]
+    with _on_device(proj):
+        ws_bytes = int(_native.lib().fmhc_k2_bwd_workspace_size(T))
+        ws = torch.empty(max(ws_bytes, 1), device=proj.device, dtype=torch.uint8)
+        _native.call("fmhc_k2_bwd_typed", proj.data_ptr(), a_pre.data_ptr(), a_post.data_ptr(),
+                     a_res.data_ptr(), bias.data_ptr(), pdt, perm.data_ptr(), qdt,
+                     g1.data_ptr(), g2.data_ptr(), g3.data_ptr(), grad_proj.data_ptr(),
+                     *(o.data_ptr() for o in outs), ws.data_ptr(), ws_bytes, T, _stream(proj))
+    return (grad_proj, *outs)
+
+
 @torch.library.impl(_lib, "fused_pre_map", "CUDA")
 def _fused_pre_map_cuda(x_streams: torch.Tensor, h_pre: torch.Tensor):
     T, n, C = x_streams.shape
@@ -521,10 +564,9 @@ def _mhc_coeffs_backward(ctx, g_hpre, g_hpost, g_H):
     g_hpre = z(T, 4) if g_hpre is None else g_hpre
     g_hpost = z(T, 4) if g_hpost is None else g_hpost
     g_H = z(T, 4, 4) if g_H is None else g_H
-    g_proj, gp = torch.ops.flash_mhc.mhc_coeffs_backward(
+    g_proj, ga_pre, ga_post, ga_res, g_bias = torch.ops.flash_mhc.mhc_coeffs_backward_split(
         g_hpre, g_hpost, g_H, proj, a_pre, a_post, a_res, bias, perm)
-    return (g_proj, gp[0:1].view_as(a_pre).to(a_pre.dtype), gp[1:2].view_as(a_post).to(a_post.dtype),
-            gp[2:3].view_as(a_res).to(a_res.dtype), gp[3:35].view_as(bias).to(bias.dtype), None)
+    return g_proj, ga_pre, ga_post, ga_res, g_bias, None
 
 
 torch.library.register_autograd(

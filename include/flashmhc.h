@@ -262,6 +262,23 @@ FMHC_API int fmhc_k2_bwd(const void *proj, const float *params, const float *per
                          const float *grad_H_merged, void *grad_proj, float *grad_params,
                          void *workspace, int64_t workspace_bytes, int64_t T, void *stream);
 
+/* ------------------------------------------------------------------------
+ * The same K2 backward with the parameters read where they live (as
+ * fmhc_k2_fwd_typed) and their gradients written in the parameters' own dtype
+ * (`param_dtype`; bf16 gradients are rounded once from the f32 sums):
+ * grad_alpha_pre, grad_alpha_post, grad_alpha_res one value each, grad_bias
+ * 32.  So a module's parameter gradients need no packing before or casts
+ * after.  Same workspace as fmhc_k2_bwd.  T == 0 writes zero gradients.
+ * No counterpart in the reference (see fmhc_k2_bwd).
+ */
+FMHC_API int fmhc_k2_bwd_typed(const void *proj, const void *alpha_pre, const void *alpha_post,
+                               const void *alpha_res, const void *bias, int param_dtype,
+                               const void *perm, int perm_dtype, const float *grad_h_pre,
+                               const float *grad_h_post, const float *grad_H_merged,
+                               void *grad_proj, void *grad_alpha_pre, void *grad_alpha_post,
+                               void *grad_alpha_res, void *grad_bias, void *workspace,
+                               int64_t workspace_bytes, int64_t T, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -138,3 +138,25 @@ def test_k2_typed_entry_matches_packed_entry(param_dtype):
     got = torch.ops.flash_mhc.mhc_coeffs(proj, *a, blk.W_all.bias, blk.perm_mat)
     for x, y in zip(got, outs[0]):
         assert torch.equal(x, y)
+
+
+@pytest.mark.parametrize("param_dtype", [torch.float32, torch.bfloat16])
+def test_k2_backward_split_matches_packed(param_dtype):
+    """mhc_coeffs_backward_split (parameters read in place, one gradient per
+    parameter written in its dtype) gives the packed op's values: the same f32
+    sums, rounded once to the parameter dtype."""
+    blk, proj = _setup(3000, 12)
+    blk = blk.to(param_dtype)
+    T = proj.shape[0]
+    g = torch.Generator(device="cuda").manual_seed(5)
+    ghp = torch.randn(T, 4, device="cuda", generator=g)
+    ghq = torch.randn(T, 4, device="cuda", generator=g)
+    gH = torch.randn(T, 4, 4, device="cuda", generator=g)
+    args = (ghp, ghq, gH, proj, blk.alpha_pre, blk.alpha_post, blk.alpha_res, blk.W_all.bias,
+            blk.perm_mat)
+    gproj_ref, gp = torch.ops.flash_mhc.mhc_coeffs_backward(*args)
+    gproj, ga, gb, gc, gbias = torch.ops.flash_mhc.mhc_coeffs_backward_split(*args)
+    assert torch.equal(gproj, gproj_ref)
+    for got, ref in ((ga, gp[0:1]), (gb, gp[1:2]), (gc, gp[2:3]), (gbias, gp[3:35])):
+        assert got.dtype == param_dtype
+        assert torch.equal(got.reshape(-1), ref.to(param_dtype))
