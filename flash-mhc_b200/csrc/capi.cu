@@ -324,6 +324,61 @@ int fmhc_k2_fwd_typed(const void *proj, const void *alpha_pre, const void *alpha
   return check_launch(w);
 }
 
+int fmhc_mhc_pre_fwd(const void *x, const void *W, const void *alpha_pre, const void *alpha_post,
+                     const void *alpha_res, const void *bias, int param_dtype, const void *perm,
+                     int perm_dtype, void *proj, float *inv_rms, float *h_pre, float *h_post,
+                     float *H_merged, void *layer_input, int64_t T, int64_t n, int64_t C,
+                     void *stream) {
+  const char *w = "fmhc_mhc_pre_fwd";
+  if (int e = check_streams(w, T, n, C)) return e;
+  const int64_t nC = n * C, D = 32;
+  if (int e = check_k1(w, T, nC, D)) return e;
+  const auto dt_ok = [](int d) { return d == FMHC_DTYPE_F32 || d == FMHC_DTYPE_BF16; };
+  if (!dt_ok(param_dtype) || !dt_ok(perm_dtype))
+    return fail(FMHC_ERR_UNSUPPORTED, "%s: parameter dtypes must be FMHC_DTYPE_F32 or FMHC_DTYPE_BF16", w);
+  if (T == 0) return ok();
+  FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, W); FMHC_REQUIRE_PTR(w, alpha_pre);
+  FMHC_REQUIRE_PTR(w, alpha_post); FMHC_REQUIRE_PTR(w, alpha_res); FMHC_REQUIRE_PTR(w, bias);
+  FMHC_REQUIRE_PTR(w, perm); FMHC_REQUIRE_PTR(w, proj); FMHC_REQUIRE_PTR(w, inv_rms);
+  FMHC_REQUIRE_PTR(w, h_pre); FMHC_REQUIRE_PTR(w, h_post); FMHC_REQUIRE_PTR(w, H_merged);
+  FMHC_REQUIRE_ALIGN2(w, x); FMHC_REQUIRE_ALIGN2(w, W); FMHC_REQUIRE_ALIGN16(w, proj);
+  FMHC_REQUIRE_ALIGN16(w, h_pre); FMHC_REQUIRE_ALIGN16(w, h_post); FMHC_REQUIRE_ALIGN16(w, H_merged);
+  if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
+  if (layer_input) FMHC_REQUIRE_ALIGN2(w, layer_input);
+  const uintptr_t pa = param_dtype == FMHC_DTYPE_BF16 ? 2 : 4;
+  const uintptr_t qa = perm_dtype == FMHC_DTYPE_BF16 ? 2 : 4;
+  if (!aligned(alpha_pre, pa) || !aligned(alpha_post, pa) || !aligned(alpha_res, pa) ||
+      !aligned(bias, pa) || !aligned(perm, qa))
+    return fail(FMHC_ERR_ALIGNMENT, "%s: parameters must be aligned to their element size", w);
+  const fmhc::K2Params P{alpha_pre, alpha_post, alpha_res, bias, perm,
+                         param_dtype == FMHC_DTYPE_BF16 ? 1 : 0,
+                         perm_dtype == FMHC_DTYPE_BF16 ? 1 : 0};
+  cudaStream_t s = (cudaStream_t)stream;
+  bool pre_done = false;
+  // K1 takes the kernel fmhc_k1_fwd would take for this call, with K2 (and
+  // at few tokens K3) in its epilogue, so every output equals the separate
+  // fmhc_k1_fwd -> fmhc_k2_fwd_typed -> fmhc_k3_fwd results bit for bit.
+  if (T <= FMHC_K1_ROWS_MAX_T && nC % 8 == 0 && aligned(x, 16) && aligned(W, 16)) {
+    const bool pre = layer_input && C % 8 == 0 && aligned(layer_input, 16);
+    fmhc::launch_k1_fwd_rows(x, W, proj, inv_rms, T, int(nC), int(D), s, &P, h_pre, h_post,
+                             H_merged, pre ? layer_input : nullptr);
+    pre_done = pre;
+  } else if (fmhc::k1_tc_fwd_supported(x, W, proj, inv_rms, T, nC, D)) {
+    if (int e = fmhc::launch_k1_tc_fwd(x, W, proj, inv_rms, T, int(nC), s, &P, h_pre, h_post,
+                                       H_merged))
+      return fail(e, "%s: %s", w, fmhc::k1_tc_error());
+  } else {
+    const int vec = pick_vec(nC, {x, W});
+    fmhc::launch_k1_fwd_simt(x, W, proj, inv_rms, T, int(nC), int(D), vec == 8 ? 8 : 1, s);
+    fmhc::launch_k2_fwd(proj, P, h_pre, h_post, H_merged, T, s);
+  }
+  if (layer_input && !pre_done) {
+    const int vec = pick_vec(C, {x, layer_input});
+    fmhc::launch_k3_fwd(x, h_pre, layer_input, T, int(C), vec, s);
+  }
+  return check_launch(w);
+}
+
 int64_t fmhc_k2_bwd_workspace_size(int64_t T) {
   if (T <= 0) return 0;
   return fmhc::k2_bwd_workspace_bytes(T);

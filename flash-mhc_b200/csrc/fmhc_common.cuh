@@ -29,6 +29,12 @@ constexpr int kWarp = 32;
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ void pdl_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
 
+// Barrier over `nthreads` threads (whole warps) of the block on barrier `id`
+// (1..15; 0 is __syncthreads()).
+__device__ __forceinline__ void named_bar_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
 // On unless the environment sets FLASH_MHC_PDL=0 (read once per process).
 inline bool pdl_enabled() {
   static const bool on = [] {

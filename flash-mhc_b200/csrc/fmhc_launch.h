@@ -30,9 +30,14 @@ void launch_k4_bwd(const void *go, const void *x, const void *lo, const float *H
 void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
                         int nC, int D, int vec, cudaStream_t s);
 // Small-T forward (block per 2 tokens, k split over the block); D == 32,
-// nC % 8 == 0, x and W 16-byte aligned.
+// nC % 8 == 0, x and W 16-byte aligned.  With `coeffs` non-null it also runs
+// K2 (writing h_pre, h_post, H, 16-byte aligned), and with `pre_out` non-null
+// also K3 into pre_out (T, nC / 4) bf16 (nC % 32 == 0, pre_out 16-byte aligned).
+struct K2Params;
 void launch_k1_fwd_rows(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
-                        int nC, int D, cudaStream_t s);
+                        int nC, int D, cudaStream_t s, const K2Params *coeffs = nullptr,
+                        float *h_pre = nullptr, float *h_post = nullptr, float *H = nullptr,
+                        void *pre_out = nullptr);
 // Largest T for which fmhc_k1_fwd takes the small-T kernel: three waves of
 // its one-block-per-SM grid on 148 SMs.  Measured at nC = 3072 (4096): 5.4
 // (6.1) us up to T = 256, 10.2 (11.8) us at 512, 18.9 (22.0) us at 1024,

@@ -13,6 +13,7 @@
 //         (deterministic), replacing src/flash_mhc/ops.py:683-684.
 #include "fmhc_common.cuh"
 #include "fmhc_launch.h"
+#include "k2_token.cuh"
 
 #include <mutex>
 
@@ -78,15 +79,28 @@ k1_fwd_simt_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
 // the tensor-core kernel walks its nC / 64 k-steps one after another, ~18 us
 // at nC = 3072 whatever T; here every block makes one pass over W.
 // Needs D == 32, nC % 8 == 0 and 16-byte aligned x and W.
+//
+// COEFFS: thread tb of the block then runs K2 on token tb's stored logits
+// (k2_token.cuh) and writes h_pre, h_post and H_merged.  PRE (with COEFFS):
+// the block then also runs K3 on its tokens, layer_input[t, c] =
+// bf16(sum_j h_pre[t, j] x[t, j, c]) with the arithmetic of k3_fwd_kernel,
+// re-reading the token rows it has just read from the caches (C % 8 == 0,
+// 16-byte aligned layer_input).  At a few tokens the whole pre-block of the
+// layer is then one launch instead of three.
 constexpr int kRowsTB = 2;
+template <bool COEFFS, bool PRE>
 __global__ void __launch_bounds__(256, 1)
 k1_fwd_rows_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
                    bf16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T, int nC,
-                   int D) {
+                   int D, const K2Params P, const k2tok::Out co, bf16 *__restrict__ pre_out) {
+  static_assert(COEFFS || !PRE, "K3 needs the coefficients");
   pdl_wait();
   __shared__ float red[8][kRowsTB][33];
   __shared__ float tot[kRowsTB][33];
+  __shared__ k2tok::ParamSmem k2s;
+  __shared__ float4 hs[kRowsTB];
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  if constexpr (COEFFS) k2tok::stage_params(k2s, P, tid, 256);  // read after the next barrier
   const int64_t t0 = int64_t(blockIdx.x) * kRowsTB;
   const bool has1 = t0 + 1 < T;
   const int nchunk = nC / 8;
@@ -167,6 +181,43 @@ k1_fwd_rows_kernel(const bf16 *__restrict__ x, const bf16 *__restrict__ W,
       const float r = rsqrtf(tot[tb][32] / float(nC) + kK1Eps);
       out[t * 32 + d] = __float2bfloat16_rn(tot[tb][d] * r);
       if (d == 0) inv_rms[t] = r;
+    }
+  }
+  if constexpr (COEFFS) {
+    if (tid < kRowsTB && t0 + tid < T) {
+      const int64_t t = t0 + tid;
+      const float r = rsqrtf(tot[tid][32] / float(nC) + kK1Eps);
+      float pv[32];  // the logits as stored above (bf16)
+#pragma unroll
+      for (int d = 0; d < 32; ++d) pv[d] = __bfloat162float(__float2bfloat16_rn(tot[tid][d] * r));
+      hs[tid] = k2tok::store_coeffs(k2s, pv, co.h_pre, co.h_post, co.H, t);
+    }
+  }
+  if constexpr (PRE) {
+    __syncthreads();
+    const int C = nC >> 2, nch = C >> 3;
+    for (int tb = 0; tb < kRowsTB; ++tb) {
+      const int64_t t = t0 + tb;
+      if (t >= T) break;
+      const float4 h = hs[tb];
+      const bf16 *xr = x + t * nC;
+      for (int c = tid; c < nch; c += 256) {
+        float f0[8], f1[8], f2[8], f3[8], o[8];
+        Chunk<8> a0, a1, a2, a3;
+        a0.v = __ldg(reinterpret_cast<const uint4 *>(xr + c * 8));
+        a1.v = __ldg(reinterpret_cast<const uint4 *>(xr + C + c * 8));
+        a2.v = __ldg(reinterpret_cast<const uint4 *>(xr + 2 * C + c * 8));
+        a3.v = __ldg(reinterpret_cast<const uint4 *>(xr + 3 * C + c * 8));
+        unpack(a0, f0); unpack(a1, f1); unpack(a2, f2); unpack(a3, f3);
+#pragma unroll
+        for (int e = 0; e < 8; ++e) {
+          float acc = h.x * f0[e];
+          acc = fmaf(h.y, f1[e], acc);
+          acc = fmaf(h.z, f2[e], acc);
+          o[e] = fmaf(h.w, f3[e], acc);
+        }
+        store_stream<8>(pre_out + t * C + c * 8, o);
+      }
     }
   }
 }
@@ -322,9 +373,14 @@ void launch_k1_fwd_simt(const void *x, const void *W, void *out, float *inv_rms,
 }
 
 void launch_k1_fwd_rows(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
-                        int nC, int D, cudaStream_t s) {
-  launch(k1_fwd_rows_kernel, dim3(unsigned((T + kRowsTB - 1) / kRowsTB)), dim3(256), 0, s,
-         (const bf16 *)x, (const bf16 *)W, (bf16 *)out, inv_rms, T, nC, D);
+                        int nC, int D, cudaStream_t s, const K2Params *coeffs, float *h_pre,
+                        float *h_post, float *H, void *pre_out) {
+  const K2Params P = coeffs ? *coeffs : K2Params{};
+  const k2tok::Out co{(float4 *)h_pre, (float4 *)h_post, (float4 *)H};
+  auto k = !coeffs ? k1_fwd_rows_kernel<false, false>
+         : pre_out ? k1_fwd_rows_kernel<true, true> : k1_fwd_rows_kernel<true, false>;
+  launch(k, dim3(unsigned((T + kRowsTB - 1) / kRowsTB)), dim3(256), 0, s, (const bf16 *)x,
+         (const bf16 *)W, (bf16 *)out, inv_rms, T, nC, D, P, co, (bf16 *)pre_out);
 }
 
 void launch_k1_bwd_dx_simt(const void *go, const void *x, const void *W, const void *proj,

@@ -33,6 +33,7 @@
 
 #include "fmhc_common.cuh"
 #include "k1_tc.h"
+#include "k2_token.cuh"
 #include "sm100_ptx.cuh"
 
 namespace fmhc {
@@ -82,16 +83,22 @@ struct alignas(1024) FwdSmem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  k2tok::ParamSmem k2;  // K2 parameters (coefficient epilogue only)
 };
 
 // Error sites recorded in g_device_error.
 enum : unsigned { kSiteProdEmpty = 0x101, kSiteMmaFull = 0x102, kSiteMmaTempty = 0x103,
                   kSiteEpiFull = 0x104, kSiteEpiTfull = 0x105, kSiteDrain = 0x106 };
 
+// COEFFS: the epilogue also runs K2 on each token's stored (bf16) logits and
+// writes h_pre, h_post and H_merged (k2_token.cuh), saving K2's launch and
+// its read of proj.
+template <bool COEFFS>
 __global__ void __launch_bounds__(kThreads, FMHC_K1F_CTAS_PER_SM)
 k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_w, __nv_bfloat16 *__restrict__ out,
-                 float *__restrict__ inv_rms, int64_t T, int nC, int64_t units) {
+                 float *__restrict__ inv_rms, int64_t T, int nC, int64_t units,
+                 const K2Params P, const k2tok::Out co) {
   extern __shared__ uint8_t smem_raw[];
   FwdSmem &sm = *reinterpret_cast<FwdSmem *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -209,6 +216,10 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     // ------------------------------------------ row warps: sumsq + epilogue
     const int q = warp & 3;  // TMEM lane quarter this warp may access
     const int r = q * 32 + lane;
+    if constexpr (COEFFS) {
+      k2tok::stage_params(sm.k2, P, int(threadIdx.x) - 64, kRowThreads);
+      named_bar_sync(1, kRowThreads);
+    }
     int stage = 0;
     uint32_t phase = 0;
     int acc = 0;
@@ -259,6 +270,7 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
         const float ss = ((ss8[0] + ss8[1]) + (ss8[2] + ss8[3])) + ((ss8[4] + ss8[5]) + (ss8[6] + ss8[7]));
         const float inv = rsqrtf(ss / float(nC) + kEps);
         uint4 *o = reinterpret_cast<uint4 *>(out + t * kND);
+        float pv[32];  // the stored bf16 logits, for the coefficient epilogue
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint4 w;
@@ -267,8 +279,13 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
           w.z = pack_bf16x2(__uint_as_float(v[8 * c + 4]) * inv, __uint_as_float(v[8 * c + 5]) * inv);
           w.w = pack_bf16x2(__uint_as_float(v[8 * c + 6]) * inv, __uint_as_float(v[8 * c + 7]) * inv);
           __stcs(o + c, w);
+          pv[8 * c + 0] = bf16lo(w.x); pv[8 * c + 1] = bf16hi(w.x);
+          pv[8 * c + 2] = bf16lo(w.y); pv[8 * c + 3] = bf16hi(w.y);
+          pv[8 * c + 4] = bf16lo(w.z); pv[8 * c + 5] = bf16hi(w.z);
+          pv[8 * c + 6] = bf16lo(w.w); pv[8 * c + 7] = bf16hi(w.w);
         }
         __stcs(inv_rms + t, inv);
+        if constexpr (COEFFS) k2tok::store_coeffs(sm.k2, pv, co.h_pre, co.h_post, co.H, t);
       }
     }
   }
@@ -311,6 +328,7 @@ struct alignas(1024) SkSmem {
   uint64_t mma_done;
   uint32_t tmem_base;
   int abort;
+  k2tok::ParamSmem k2;         // K2 parameters (coefficient epilogue, rank 0 only)
 };
 
 enum : unsigned { kSiteSkProdEmpty = 0x111, kSiteSkMmaFull = 0x112, kSiteSkRowFull = 0x113,
@@ -324,11 +342,13 @@ __device__ __forceinline__ void sk_send(SkSmem &sm, const float (&acc)[33], int 
   mbar_arrive_remote(mapa_shared(smem_u32(&sm.rfull[slot]), dst));
 }
 
+// COEFFS: as in k1_fwd_tc_kernel, rank 0's epilogue also runs K2.
+template <bool COEFFS>
 __global__ void __launch_bounds__(kThreads, FMHC_K1F_CTAS_PER_SM)
 k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_w,
                         __nv_bfloat16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T,
-                        int nC, int S) {
+                        int nC, int S, const K2Params P, const k2tok::Out co) {
   extern __shared__ uint8_t smem_raw[];
   SkSmem &sm = *reinterpret_cast<SkSmem *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -426,6 +446,12 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
     // ---------------------------------- row warps: sumsq, partial, tree
     const int q = warp & 3;
     const int r = q * 32 + lane;
+    if constexpr (COEFFS) {
+      if (rank == 0) {
+        k2tok::stage_params(sm.k2, P, int(threadIdx.x) - 64, kRowThreads);
+        named_bar_sync(1, kRowThreads);
+      }
+    }
     int stage = 0;
     uint32_t phase = 0;
     float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -487,6 +513,7 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
         const int64_t t = row0 + r;
         const float inv = rsqrtf(acc[32] / float(nC) + kEps);
         uint4 *o = reinterpret_cast<uint4 *>(out + t * kND);
+        float pv[32];
 #pragma unroll
         for (int c = 0; c < 4; ++c) {
           uint4 w;
@@ -495,8 +522,13 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
           w.z = pack_bf16x2(acc[8 * c + 4] * inv, acc[8 * c + 5] * inv);
           w.w = pack_bf16x2(acc[8 * c + 6] * inv, acc[8 * c + 7] * inv);
           __stcs(o + c, w);
+          pv[8 * c + 0] = bf16lo(w.x); pv[8 * c + 1] = bf16hi(w.x);
+          pv[8 * c + 2] = bf16lo(w.y); pv[8 * c + 3] = bf16hi(w.y);
+          pv[8 * c + 4] = bf16lo(w.z); pv[8 * c + 5] = bf16hi(w.z);
+          pv[8 * c + 6] = bf16lo(w.w); pv[8 * c + 7] = bf16hi(w.w);
         }
         __stcs(inv_rms + t, inv);
+        if constexpr (COEFFS) k2tok::store_coeffs(sm.k2, pv, co.h_pre, co.h_post, co.H, t);
       }
     }
   }
@@ -617,8 +649,12 @@ bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const fl
 }
 
 int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t T, int nC,
-                     cudaStream_t s) {
+                     cudaStream_t s, const K2Params *coeffs, float *h_pre, float *h_post,
+                     float *H) {
   using namespace k1tc;
+  const K2Params P = coeffs ? *coeffs : K2Params{};
+  const k2tok::Out co{reinterpret_cast<float4 *>(h_pre), reinterpret_cast<float4 *>(h_post),
+                      reinterpret_cast<float4 *>(H)};
   // Few 128-row tiles: split k over clusters of S CTAs.  Measured (profiler
   // kernel times, nC = 4096; nC = 3072 alike): S = 4 while the clusters fit
   // one CTA per SM (T <= 4736: 24 -> 18.6 us at T = 1024..4096); S = 2 while
@@ -646,11 +682,11 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
         return 5;
       }
       const size_t smem = sizeof(SkSmem) + 1024;
-      if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_splitk_kernel), smem))
-        return e;
-      if (launch_cluster(k1_fwd_tc_splitk_kernel, dim3(unsigned(tiles * S)), dim3(kThreads), smem,
-                         s, unsigned(S), mx, mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms,
-                         T, nC, S) != cudaSuccess) {
+      auto kern = coeffs ? k1_fwd_tc_splitk_kernel<true> : k1_fwd_tc_splitk_kernel<false>;
+      if (int e = set_smem_attr(reinterpret_cast<const void *>(kern), smem)) return e;
+      if (launch_cluster(kern, dim3(unsigned(tiles * S)), dim3(kThreads), smem, s, unsigned(S), mx,
+                         mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, S, P,
+                         co) != cudaSuccess) {
         snprintf(g_msg, sizeof(g_msg), "cluster launch of the split-K K1 forward failed");
         return 4;
       }
@@ -669,9 +705,10 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
   int64_t grid = int64_t(device_sms()) * FMHC_K1F_CTAS_PER_SM;
   if (grid > units) grid = units;
   const size_t smem = sizeof(FwdSmem) + 1024;
-  if (int e = set_smem_attr(reinterpret_cast<const void *>(k1_fwd_tc_kernel), smem)) return e;
-  launch(k1_fwd_tc_kernel, dim3(unsigned(grid)), dim3(kThreads), smem, s, mx, mw,
-         reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units);
+  auto kern = coeffs ? k1_fwd_tc_kernel<true> : k1_fwd_tc_kernel<false>;
+  if (int e = set_smem_attr(reinterpret_cast<const void *>(kern), smem)) return e;
+  launch(kern, dim3(unsigned(grid)), dim3(kThreads), smem, s, mx, mw,
+         reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units, P, co);
   return 0;
 }
 

@@ -4,6 +4,8 @@
 #include <cuda_runtime.h>
 #include <stdint.h>
 
+#include "fmhc_launch.h"
+
 namespace fmhc {
 
 // True when the tensor-core forward kernel handles this call (shape, alignment,
@@ -11,8 +13,11 @@ namespace fmhc {
 bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
                          int64_t T, int64_t nC, int64_t D);
 // Returns 0 or an fmhc_status code; k1_tc_error() then describes the failure.
+// With `coeffs` non-null the epilogue also runs K2 (parameters *coeffs) and
+// writes h_pre, h_post (T, 4) and H_merged (T, 4, 4), each 16-byte aligned.
 int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t T, int nC,
-                     cudaStream_t s);
+                     cudaStream_t s, const K2Params *coeffs = nullptr, float *h_pre = nullptr,
+                     float *h_post = nullptr, float *H = nullptr);
 const char *k1_tc_error();
 
 // Backward (grad_x, and grad_W when gW != nullptr) on the tensor cores.

@@ -1,27 +1,14 @@
 // K2: the per-token coefficient math of mHC-lite, forward and backward, as one
 // kernel each (the reference runs it as ~20 eager torch launches in the
-// caller, src/flash_mhc/block.py:150-170).
-//
-// Per token, from the 32 projection logits proj = [p (4) | q (4) | r (24)]:
-//   h_pre   = sigmoid(a_pre * p + b[0:4])
-//   h_post  = 2 * sigmoid(a_post * q + b[4:8])
-//   a       = softmax(a_res * r + b[8:32])              (over the 24 entries)
-//   H_res   = sum_k a[k] * perm[k]                      (4x4, perm rows are the
-//                                                        flattened permutation matrices)
-//   H_merged= H_res - h_post (outer) h_pre
-// The reference evaluates this in the input dtype (bf16): alphas and bias are
-// cast to bf16 and h_pre, h_post, H_merged are stored as bf16 before the
-// f32 copies that K3/K4 consume.  Here the parameters are rounded to bf16 the
-// same way and the three outputs are rounded to bf16 (then stored as f32),
-// while the intermediate arithmetic runs in f32 (the reference rounds every
-// intermediate op to bf16; the results agree to bf16 rounding).
+// caller, src/flash_mhc/block.py:150-170).  The per-token forward and its
+// rounding rules live in k2_token.cuh (shared with the K1 forward kernels
+// that run it in their epilogue).
 //
 // The backward takes the f32 gradients of h_pre (from K3's backward), h_post
 // and H_merged (from K4's backward), recomputes the forward intermediates from
 // proj and returns grad_proj (bf16, the dtype of proj) plus the parameter
 // gradients (3 alphas, 32 bias entries) summed over tokens in a fixed order.
-#include "fmhc_common.cuh"
-#include "fmhc_launch.h"
+#include "k2_token.cuh"
 
 namespace fmhc {
 
@@ -29,32 +16,13 @@ using bf16 = __nv_bfloat16;
 
 namespace {
 
-constexpr int kP = 35;  // a_pre, a_post, a_res, bias[32]
-constexpr int kNF = 24; // permutations of 4
-
-__device__ __forceinline__ float bf16r(float v) { return __bfloat162float(__float2bfloat16_rn(v)); }
-__device__ __forceinline__ float sigm(float z) { return 1.f / (1.f + __expf(-z)); }
-
-struct K2Smem {
-  float par[kP];
-  float perm[kNF * 16];
-};
-
-__device__ __forceinline__ float ld_param(const void *p, int i, int is_bf16) {
-  return is_bf16 ? __bfloat162float(reinterpret_cast<const bf16 *>(p)[i])
-                 : reinterpret_cast<const float *>(p)[i];
-}
+using k2tok::kP;
+using k2tok::kNF;
+using K2Smem = k2tok::ParamSmem;
+using K2Tok = k2tok::Tok;
 
 __device__ __forceinline__ void load_params(K2Smem &sm, const K2Params &P) {
-  for (int i = threadIdx.x; i < kP; i += blockDim.x) {
-    const float v = i == 0 ? ld_param(P.a_pre, 0, P.param_bf16)
-                  : i == 1 ? ld_param(P.a_post, 0, P.param_bf16)
-                  : i == 2 ? ld_param(P.a_res, 0, P.param_bf16)
-                           : ld_param(P.bias, i - 3, P.param_bf16);
-    sm.par[i] = bf16r(v);
-  }
-  for (int i = threadIdx.x; i < kNF * 16; i += blockDim.x)
-    sm.perm[i] = bf16r(ld_param(P.perm, i, P.perm_bf16));
+  k2tok::stage_params(sm, P, threadIdx.x, blockDim.x);
   __syncthreads();
 }
 
@@ -70,40 +38,6 @@ __device__ __forceinline__ void load_proj(const bf16 *proj, int64_t t, float (&v
   }
 }
 
-// Forward intermediates of one token.
-struct K2Tok {
-  float spre[4], spost[4];  // sigmoids (unrounded)
-  float hpre[4], hpost[4];  // bf16-rounded outputs
-  float a[kNF];             // softmax
-};
-
-__device__ __forceinline__ void k2_forward_token(const K2Smem &sm, const float (&v)[32], K2Tok &k) {
-  const float ap = sm.par[0], aq = sm.par[1], ar = sm.par[2];
-  const float *b = sm.par + 3;
-#pragma unroll
-  for (int i = 0; i < 4; ++i) {
-    k.spre[i] = sigm(ap * v[i] + b[i]);
-    k.hpre[i] = bf16r(k.spre[i]);
-    k.spost[i] = sigm(aq * v[4 + i] + b[4 + i]);
-    k.hpost[i] = bf16r(2.f * k.spost[i]);
-  }
-  float m = -INFINITY;
-#pragma unroll
-  for (int j = 0; j < kNF; ++j) {
-    k.a[j] = ar * v[8 + j] + b[8 + j];
-    m = fmaxf(m, k.a[j]);
-  }
-  float s = 0.f;
-#pragma unroll
-  for (int j = 0; j < kNF; ++j) {
-    k.a[j] = __expf(k.a[j] - m);
-    s += k.a[j];
-  }
-  const float inv = 1.f / s;
-#pragma unroll
-  for (int j = 0; j < kNF; ++j) k.a[j] *= inv;
-}
-
 }  // namespace
 
 __global__ void __launch_bounds__(256)
@@ -116,21 +50,7 @@ k2_fwd_kernel(const bf16 *__restrict__ proj, const K2Params P, float4 *__restric
   if (t < T) load_proj(proj, t, v);  // in flight while the parameters are staged
   load_params(sm, P);
   if (t >= T) return;
-  K2Tok k;
-  k2_forward_token(sm, v, k);
-  float Hm[16];
-#pragma unroll
-  for (int e = 0; e < 16; ++e) {
-    float acc = 0.f;  // bf16 softmax output times the bf16 permutation rows, f32 accumulate
-#pragma unroll
-    for (int j = 0; j < kNF; ++j) acc = fmaf(bf16r(k.a[j]), sm.perm[j * 16 + e], acc);
-    Hm[e] = bf16r(bf16r(acc) - bf16r(k.hpost[e >> 2] * k.hpre[e & 3]));
-  }
-  h_pre[t] = make_float4(k.hpre[0], k.hpre[1], k.hpre[2], k.hpre[3]);
-  h_post[t] = make_float4(k.hpost[0], k.hpost[1], k.hpost[2], k.hpost[3]);
-#pragma unroll
-  for (int i = 0; i < 4; ++i)
-    H[t * 4 + i] = make_float4(Hm[4 * i + 0], Hm[4 * i + 1], Hm[4 * i + 2], Hm[4 * i + 3]);
+  k2tok::store_coeffs(sm, v, h_pre, h_post, H, t);
 }
 
 // One thread per token; each block writes the sums of its tokens' parameter
@@ -151,7 +71,7 @@ k2_bwd_kernel(const bf16 *__restrict__ proj, const K2Params P, const float4 *__r
     float v[32];
     load_proj(proj, t, v);
     K2Tok k;
-    k2_forward_token(sm, v, k);
+    k2tok::forward_token(sm, v, k);
     const float4 a4 = g_hpre[t], b4 = g_hpost[t];
     float ghpre[4] = {a4.x, a4.y, a4.z, a4.w};
     float ghpost[4] = {b4.x, b4.y, b4.z, b4.w};

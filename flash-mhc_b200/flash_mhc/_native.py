@@ -36,6 +36,8 @@ _SIGNATURES = {
                           _i64, _vp],
     "fmhc_k2_bwd_typed": [_vp, _vp, _vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp, _vp,
                           _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
+    "fmhc_mhc_pre_fwd": [_vp, _vp, _vp, _vp, _vp, _vp, ctypes.c_int, _vp, ctypes.c_int, _vp, _vp,
+                         _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k2_bwd_workspace_size": [_i64],
     "fmhc_k2_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "fmhc_k3_fwd": [_vp, _vp, _vp, _i64, _i64, _i64, _vp],

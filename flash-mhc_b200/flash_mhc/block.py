@@ -57,7 +57,9 @@ class _StreamGrad:
 
 
 class _FusedPreMap(torch.autograd.Function):
-    """K1 (RMSNorm + projection), K2 (coefficients), K3 (pre-map) forward.
+    """K1 (RMSNorm + projection), K2 (coefficients), K3 (pre-map) forward, as
+    one ``mhc_pre_forward`` call (K2 runs in K1's epilogue; at few tokens K3
+    too, one launch in all).
 
     Backward from saved tensors only (no forward kernel is re-run):
     K3's grad_h_pre -> K2 bwd -> K1 bwd (grad_x and grad_W in one pass), then
@@ -69,9 +71,8 @@ class _FusedPreMap(torch.autograd.Function):
     def forward(ctx, x, W, a_pre, a_post, a_res, bias, perm, slot):
         ops = torch.ops.flash_mhc
         T, n, C = x.shape
-        proj, inv = ops.fused_rmsnorm_project(x.reshape(T, n * C), W)
-        h_pre, h_post, H = ops.mhc_coeffs(proj, a_pre, a_post, a_res, bias, perm)
-        layer_input = ops.fused_pre_map(x, h_pre)
+        layer_input, proj, inv, h_pre, h_post, H = ops.mhc_pre_forward(
+            x, W, a_pre, a_post, a_res, bias, perm)
         ctx.save_for_backward(x, W, proj, inv, h_pre, a_pre, a_post, a_res, bias, perm)
         ctx.slot = slot
         return layer_input, H, h_post
@@ -252,15 +253,13 @@ class MHCLiteBlock(nn.Module):
         """Inference (grad disabled, not under torch.compile): the same kernels
         called without the autograd Functions and the op dispatcher, whose host
         cost dominates at small T (~200 -> ~70 us per forward at T = 1)."""
-        T = x_streams.shape[0]
         dt = x_streams.dtype
         W = self.W_all.weight
         if W.dtype != dt:
             W = W.to(dt)
-        proj, _inv = _ops._fused_rmsnorm_project_cuda(x_streams.reshape(T, self.nC), W)
-        h_pre, h_post, H_merged = _ops._mhc_coeffs_cuda(
-            proj, self.alpha_pre, self.alpha_post, self.alpha_res, self.W_all.bias, self.perm_mat)
-        layer_input = _ops._fused_pre_map_cuda(x_streams, h_pre)
+        layer_input, _proj, _inv, _h_pre, h_post, H_merged = _ops._mhc_pre_forward_cuda(
+            x_streams, W, self.alpha_pre, self.alpha_post, self.alpha_res, self.W_all.bias,
+            self.perm_mat)
         layer_output = self.layer(layer_input, **kwargs)
         return _ops._fused_post_res_cuda(x_streams, layer_output, H_merged, h_post)
 

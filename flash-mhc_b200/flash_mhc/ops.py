@@ -52,6 +52,12 @@ _lib.define(
 _lib.define(
     "mhc_coeffs(Tensor proj, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor h_pre, Tensor h_post, Tensor H_merged)"
 )
+# Not in the reference: the block's pre-map forward in one call -- K1 with K2
+# in its epilogue, then K3 (at few tokens all three in one kernel); replaces
+# block.py:150-177 (_mhc_coeffs_triton + _mhc_pre_map_triton).
+_lib.define(
+    "mhc_pre_forward(Tensor x_streams, Tensor W, Tensor alpha_pre, Tensor alpha_post, Tensor alpha_res, Tensor bias, Tensor perm) -> (Tensor layer_input, Tensor proj, Tensor inv_rms, Tensor h_pre, Tensor h_post, Tensor H_merged)"
+)
 # Not in the reference: pieces of the fused block backward.
 _lib.define("pre_map_grad_h(Tensor grad_out, Tensor x_streams, Tensor h_pre) -> Tensor grad_h_pre")
 _lib.define(
@@ -132,6 +138,16 @@ def _mhc_coeffs_fake(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
     T = proj.shape[0]
     f = dict(device=proj.device, dtype=torch.float32)
     return torch.empty((T, 4), **f), torch.empty((T, 4), **f), torch.empty((T, 4, 4), **f)
+
+
+@torch.library.register_fake("flash_mhc::mhc_pre_forward")
+def _mhc_pre_forward_fake(x_streams, W, alpha_pre, alpha_post, alpha_res, bias, perm):
+    T, n, C = x_streams.shape
+    f = dict(device=x_streams.device, dtype=torch.float32)
+    return (torch.empty((T, C), device=x_streams.device, dtype=x_streams.dtype),
+            torch.empty((T, W.shape[0]), device=x_streams.device, dtype=x_streams.dtype),
+            torch.empty((T,), **f), torch.empty((T, 4), **f), torch.empty((T, 4), **f),
+            torch.empty((T, 4, 4), **f))
 
 
 @torch.library.register_fake("flash_mhc::mhc_coeffs_backward")
@@ -309,23 +325,33 @@ def _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
 _K2_DTYPES = {torch.float32: 0, torch.bfloat16: 1}  # FMHC_DTYPE_F32, FMHC_DTYPE_BF16
 
 
-@torch.library.impl(_lib, "mhc_coeffs", "CUDA")
-def _mhc_coeffs_cuda(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
+def _k2_typed_args(alpha_pre, alpha_post, alpha_res, bias, perm):
+    """Pointer arguments of the typed K2 entries, and the tensors they point into.
+
+    f32 or bf16 parameters of one dtype are passed as they are (the kernel
+    reads them in their own dtype); anything else is packed to f32 first."""
+    if bias.numel() != 32 or perm.shape != (24, 16):
+        raise ValueError("flash_mhc::mhc_coeffs: bias must have 32 entries and perm be (24, 16)")
     pdt, qdt = _K2_DTYPES.get(bias.dtype), _K2_DTYPES.get(perm.dtype)
     same = all(a.dtype == bias.dtype for a in (alpha_pre, alpha_post, alpha_res))
-    if pdt is None or qdt is None or not same or proj.dim() != 2 or proj.shape[1] != 32 \
-            or bias.numel() != 32 or perm.shape != (24, 16):
-        # Other dtypes or shapes: pack to f32 (and validate) first.
-        proj, params, perm = _k2_params(proj, alpha_pre, alpha_post, alpha_res, bias, perm)
-        args = (params.data_ptr(), params.data_ptr() + 4, params.data_ptr() + 8,
-                params.data_ptr() + 12, 0, perm.data_ptr(), 0)
-    else:
-        # The parameters as they are: the kernel reads them in their own dtype.
-        proj = _bf16("proj", proj)
-        a_pre, a_post, a_res = (a.contiguous() for a in (alpha_pre, alpha_post, alpha_res))
-        bias, perm = bias.contiguous(), perm.contiguous()
-        args = (a_pre.data_ptr(), a_post.data_ptr(), a_res.data_ptr(), bias.data_ptr(), pdt,
-                perm.data_ptr(), qdt)
+    if pdt is None or qdt is None or not same:
+        params = torch.cat([alpha_pre.reshape(-1)[:1], alpha_post.reshape(-1)[:1],
+                            alpha_res.reshape(-1)[:1], bias.reshape(-1)]).to(torch.float32).contiguous()
+        perm = perm.to(torch.float32).contiguous()
+        p = params.data_ptr()
+        return (p, p + 4, p + 8, p + 12, 0, perm.data_ptr(), 0), (params, perm)
+    a_pre, a_post, a_res = (a.contiguous() for a in (alpha_pre, alpha_post, alpha_res))
+    bias, perm = bias.contiguous(), perm.contiguous()
+    return ((a_pre.data_ptr(), a_post.data_ptr(), a_res.data_ptr(), bias.data_ptr(), pdt,
+             perm.data_ptr(), qdt), (a_pre, a_post, a_res, bias, perm))
+
+
+@torch.library.impl(_lib, "mhc_coeffs", "CUDA")
+def _mhc_coeffs_cuda(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
+    if proj.dim() != 2 or proj.shape[1] != 32:
+        raise ValueError(f"flash_mhc::mhc_coeffs: proj must be (T, 32) (n=4), got {tuple(proj.shape)}")
+    proj = _bf16("proj", proj)
+    args, _keep = _k2_typed_args(alpha_pre, alpha_post, alpha_res, bias, perm)
     T = proj.shape[0]
     f = dict(device=proj.device, dtype=torch.float32)
     h_pre, h_post, H = torch.empty((T, 4), **f), torch.empty((T, 4), **f), torch.empty((T, 4, 4), **f)
@@ -333,6 +359,28 @@ def _mhc_coeffs_cuda(proj, alpha_pre, alpha_post, alpha_res, bias, perm):
         _native.call("fmhc_k2_fwd_typed", proj.data_ptr(), *args, h_pre.data_ptr(),
                      h_post.data_ptr(), H.data_ptr(), T, _stream(proj))
     return h_pre, h_post, H
+
+
+@torch.library.impl(_lib, "mhc_pre_forward", "CUDA")
+def _mhc_pre_forward_cuda(x_streams, W, alpha_pre, alpha_post, alpha_res, bias, perm):
+    T, n, C = x_streams.shape
+    _n4("mhc_pre_forward", n)
+    x_streams = _bf16("x_streams", x_streams)
+    W = _bf16("W", W)
+    if tuple(W.shape) != (32, n * C):
+        raise ValueError(f"flash_mhc::mhc_pre_forward: W must be (32, {n * C}), got {tuple(W.shape)}")
+    args, _keep = _k2_typed_args(alpha_pre, alpha_post, alpha_res, bias, perm)
+    dev, dt = x_streams.device, x_streams.dtype
+    f = dict(device=dev, dtype=torch.float32)
+    layer_input = torch.empty((T, C), device=dev, dtype=dt)
+    proj = torch.empty((T, 32), device=dev, dtype=dt)
+    inv_rms = torch.empty((T,), **f)
+    h_pre, h_post, H = torch.empty((T, 4), **f), torch.empty((T, 4), **f), torch.empty((T, 4, 4), **f)
+    with _on_device(x_streams):
+        _native.call("fmhc_mhc_pre_fwd", x_streams.data_ptr(), W.data_ptr(), *args,
+                     proj.data_ptr(), inv_rms.data_ptr(), h_pre.data_ptr(), h_post.data_ptr(),
+                     H.data_ptr(), layer_input.data_ptr(), T, n, C, _stream(x_streams))
+    return layer_input, proj, inv_rms, h_pre, h_post, H
 
 
 @torch.library.impl(_lib, "mhc_coeffs_backward", "CUDA")

@@ -250,6 +250,28 @@ FMHC_API int fmhc_k2_fwd_typed(const void *proj, const void *alpha_pre, const vo
                                float *H_merged, int64_t T, void *stream);
 
 /* ------------------------------------------------------------------------
+ * The pre-block of an mHC-lite layer in one call: K1 (x (T, n, C) bf16 as
+ * x_flat (T, nC), W (32, nC) bf16 -> proj (T, 32) bf16, inv_rms (T,) f32),
+ * K2 on proj (parameters as in fmhc_k2_fwd_typed -> h_pre, h_post (T, 4),
+ * H_merged (T, 4, 4) f32) and, when layer_input is not NULL, K3
+ * (layer_input (T, C) bf16 = pre-map of x with h_pre).  K1 runs the kernel
+ * fmhc_k1_fwd would run, with K2 in its epilogue (no launch and no read of
+ * proj for K2); for T <= 888 with C % 8 == 0 and 16-byte aligned x, W and
+ * layer_input, K3 runs in the same kernel too (one launch in all).  Every
+ * output is bit-identical to fmhc_k1_fwd -> fmhc_k2_fwd_typed -> fmhc_k3_fwd.
+ * proj, h_pre, h_post and H_merged 16-byte aligned; n == 4.
+ * Replaces the reference's MHCLiteBlock._mhc_pre_map_triton
+ * (src/flash_mhc/block.py:172-177 with _mhc_coeffs_triton, 150-170): its
+ * fused_rmsnorm_project (ops.py:205-264), eager coefficient math and
+ * fused_pre_map (ops.py:347-414) calls.
+ */
+FMHC_API int fmhc_mhc_pre_fwd(const void *x, const void *W, const void *alpha_pre,
+                              const void *alpha_post, const void *alpha_res, const void *bias,
+                              int param_dtype, const void *perm, int perm_dtype, void *proj,
+                              float *inv_rms, float *h_pre, float *h_post, float *H_merged,
+                              void *layer_input, int64_t T, int64_t n, int64_t C, void *stream);
+
+/* ------------------------------------------------------------------------
  * K2 backward: given the f32 gradients of h_pre, h_post and H_merged, returns
  * grad_proj (T, 32) bf16 and grad_params (35,) f32 (summed over tokens in a
  * fixed order, deterministic).  `workspace` (256-byte aligned) holds per-block

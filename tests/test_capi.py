@@ -65,6 +65,21 @@ def test_argument_validation_without_gpu():
     assert st == 2 and "dtype" in msg
     st, msg = _status("fmhc_mhc_grad_x_combine_post", p, p, p, p, p, p, 8, 3, 64, None)
     assert st == 1 and "n=4" in msg
+    # the pre-block entry (K1 + K2 + K3): n, dtype, NULL and alignment checks
+    pre = lambda **kw: _status("fmhc_mhc_pre_fwd", *[kw.get(k, d) for k, d in (  # noqa: E731
+        ("x", p), ("W", p), ("a_pre", p), ("a_post", p), ("a_res", p), ("bias", p), ("pdt", 0),
+        ("perm", p), ("qdt", 0), ("proj", p), ("inv", p), ("h_pre", p), ("h_post", p), ("H", p),
+        ("li", p), ("T", 8), ("n", 4), ("C", 64), ("stream", None))])
+    st, msg = pre(n=3)
+    assert st == 1 and "n=4" in msg
+    st, msg = pre(pdt=5)
+    assert st == 2 and "dtype" in msg
+    st, msg = pre(proj=None)
+    assert st == 1 and "NULL" in msg
+    st, msg = pre(h_pre=ctypes.c_void_p(20))
+    assert st == 3 and "16-byte" in msg
+    st, msg = pre(x=None, W=None, proj=None, T=0)
+    assert st == 0 and msg == ""
     # K4 backward accepts grad_x = NULL (parameter gradients only); the other
     # outputs are still required
     st, msg = _status("fmhc_k4_bwd", p, p, p, p, p, None, None, p, p, 8, 4, 64, None)

@@ -52,7 +52,7 @@ def test_k2_forward_matches_reference_eager_bf16(T, scale):
 
 
 def _oracle_params(blk):
-    return dict(ap=float(blk.alpha_pre), aq=float(blk.alpha_post), ar=float(blk.alpha_res),
+    return dict(ap=blk.alpha_pre.item(), aq=blk.alpha_post.item(), ar=blk.alpha_res.item(),
                 bias=O.bf16_round(blk.W_all.bias.detach().float().cpu().numpy()),
                 perm=blk.perm_mat.float().cpu().numpy())
 
@@ -61,7 +61,7 @@ def _oracle_params(blk):
 def test_k2_forward_backward_match_float64_oracle(T):
     blk, proj = _setup(T, 2)
     p = _oracle_params(blk)
-    ap, aq, ar = (float(O.bf16_round(np.float32(v))) for v in (p["ap"], p["aq"], p["ar"]))
+    ap, aq, ar = (float(O.bf16_round(np.float32(v)).reshape(-1)[0]) for v in (p["ap"], p["aq"], p["ar"]))
     pr = proj.float().cpu().numpy()
     ctx = O.k2_coeffs(pr, ap, aq, ar, p["bias"], p["perm"])
     with torch.no_grad():
