@@ -200,9 +200,12 @@ int fmhc_k1_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t
   if (!aligned(inv_rms, 4)) return fail(FMHC_ERR_ALIGNMENT, "%s: inv_rms must be 4-byte aligned", w);
   cudaStream_t s = (cudaStream_t)stream;
   if (T <= FMHC_K1_ROWS_MAX_T && D == 32 && nC % 8 == 0 && aligned(x, 16) && aligned(W, 16)) {
-    // Few tokens: one pass over W per block of 4 tokens beats the tensor-core
+    // Few tokens: one pass over W per block of 2 tokens (split over a cluster
+    // while the tokens are too few to fill the GPU) beats the tensor-core
     // kernel's serial k-loop per tile.
-    fmhc::launch_k1_fwd_rows(x, W, out, inv_rms, T, int(nC), int(D), s);
+    const int rc = fmhc::launch_k1_fwd_rows_cluster(x, W, out, inv_rms, T, int(nC), s);
+    if (rc > 0) return fail(rc, "%s: %s", w, fmhc::k1_tc_error());
+    if (rc < 0) fmhc::launch_k1_fwd_rows(x, W, out, inv_rms, T, int(nC), int(D), s);
   } else if (fmhc::k1_tc_fwd_supported(x, W, out, inv_rms, T, nC, D)) {
     if (int e = fmhc::launch_k1_tc_fwd(x, W, out, inv_rms, T, int(nC), s))
       return fail(e, "%s: %s", w, fmhc::k1_tc_error());
@@ -360,8 +363,13 @@ int fmhc_mhc_pre_fwd(const void *x, const void *W, const void *alpha_pre, const 
   // fmhc_k1_fwd -> fmhc_k2_fwd_typed -> fmhc_k3_fwd results bit for bit.
   if (T <= FMHC_K1_ROWS_MAX_T && nC % 8 == 0 && aligned(x, 16) && aligned(W, 16)) {
     const bool pre = layer_input && C % 8 == 0 && aligned(layer_input, 16);
-    fmhc::launch_k1_fwd_rows(x, W, proj, inv_rms, T, int(nC), int(D), s, &P, h_pre, h_post,
-                             H_merged, pre ? layer_input : nullptr);
+    void *pre_out = pre ? layer_input : nullptr;
+    const int rc = fmhc::launch_k1_fwd_rows_cluster(x, W, proj, inv_rms, T, int(nC), s, &P, h_pre,
+                                                    h_post, H_merged, pre_out);
+    if (rc > 0) return fail(rc, "%s: %s", w, fmhc::k1_tc_error());
+    if (rc < 0)
+      fmhc::launch_k1_fwd_rows(x, W, proj, inv_rms, T, int(nC), int(D), s, &P, h_pre, h_post,
+                               H_merged, pre_out);
     pre_done = pre;
   } else if (fmhc::k1_tc_fwd_supported(x, W, proj, inv_rms, T, nC, D)) {
     if (int e = fmhc::launch_k1_tc_fwd(x, W, proj, inv_rms, T, int(nC), s, &P, h_pre, h_post,

@@ -316,13 +316,20 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
 // acquire) and adds.  Senders then exit: no CTA reads another's buffer after
 // its owner may have left.  Rank 0 finishes: inv_rms = rsqrt(ss / nC + eps),
 // out = bf16(proj * inv_rms).  Nothing here addresses another GPU.
-constexpr int kSkStages = 3;
+//
+// Pipeline depth ST: with at most one CTA per SM (clusters x S <= SMs) each
+// CTA streams its k-steps through kSkStagesDeep stages (160 KiB in flight:
+// the k-loop is bound by the TMA round trip, not by bandwidth); with more CTAs
+// two share an SM and each gets kSkStagesShallow.
+constexpr int kSkStagesShallow = 3;
+constexpr int kSkStagesDeep = 8;
 constexpr int kSkRows = 128;
+template <int ST>
 struct alignas(1024) SkSmem {
-  uint8_t stage[kSkStages][kStageBytes];
+  uint8_t stage[ST][kStageBytes];
   float recv[2][kSkRows][33];  // partials received at the first and second level
-  uint64_t full[kSkStages];
-  uint64_t empty[kSkStages];
+  uint64_t full[ST];
+  uint64_t empty[ST];
   uint64_t tfull;
   uint64_t rfull[2];           // 128 remote arrivals (one per sender row thread)
   uint64_t mma_done;
@@ -334,7 +341,8 @@ struct alignas(1024) SkSmem {
 enum : unsigned { kSiteSkProdEmpty = 0x111, kSiteSkMmaFull = 0x112, kSiteSkRowFull = 0x113,
                   kSiteSkTfull = 0x114, kSiteSkRecv = 0x115, kSiteSkDrain = 0x116 };
 
-__device__ __forceinline__ void sk_send(SkSmem &sm, const float (&acc)[33], int r, int slot,
+template <int ST>
+__device__ __forceinline__ void sk_send(SkSmem<ST> &sm, const float (&acc)[33], int r, int slot,
                                         uint32_t dst) {
   const uint32_t base = mapa_shared(smem_u32(&sm.recv[slot][r][0]), dst);
 #pragma unroll
@@ -343,14 +351,14 @@ __device__ __forceinline__ void sk_send(SkSmem &sm, const float (&acc)[33], int 
 }
 
 // COEFFS: as in k1_fwd_tc_kernel, rank 0's epilogue also runs K2.
-template <bool COEFFS>
+template <bool COEFFS, int ST>
 __global__ void __launch_bounds__(kThreads, FMHC_K1F_CTAS_PER_SM)
 k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
                         const __grid_constant__ CUtensorMap tmap_w,
                         __nv_bfloat16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T,
                         int nC, int S, const K2Params P, const k2tok::Out co) {
   extern __shared__ uint8_t smem_raw[];
-  SkSmem &sm = *reinterpret_cast<SkSmem *>(
+  SkSmem<ST> &sm = *reinterpret_cast<SkSmem<ST> *>(
       (reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -363,7 +371,7 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int kb0 = int(rank) * nk / S, kb1 = (int(rank) + 1) * nk / S;
 
   if (threadIdx.x == 0) {
-    for (int st = 0; st < kSkStages; ++st) {
+    for (int st = 0; st < ST; ++st) {
       mbar_init(smem_u32(&sm.full[st]), 1);
       mbar_init(smem_u32(&sm.empty[st]), 1 + kRowThreads);
     }
@@ -407,13 +415,13 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
           tma_load_2d(a + kABytes + cb * kColBBytes, &tmap_w, full, k0, 0);
         }
         ++issued;
-        if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+        if (++stage == ST) { stage = 0; phase ^= 1; }
       }
-      int n = issued < kSkStages ? issued : kSkStages;
+      int n = issued < ST ? issued : ST;
       int st = stage;
       uint32_t ph = phase;
       for (int i = 0; i < n; ++i) {
-        if (--st < 0) { st = kSkStages - 1; ph ^= 1; }
+        if (--st < 0) { st = ST - 1; ph ^= 1; }
         mbar_wait(smem_u32(&sm.full[st]), ph, abort, kSiteSkDrain, true);
       }
     }
@@ -436,7 +444,7 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
           mma_bf16_ss(tmem, ad, bd, idesc, (kb != kb0 || k != 0) ? 1u : 0u);
         }
         mma_commit(smem_u32(&sm.empty[stage]));
-        if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+        if (++stage == ST) { stage = 0; phase ^= 1; }
       }
       if (ok) mma_commit(smem_u32(&sm.tfull));
       mma_commit(smem_u32(&sm.mma_done));
@@ -475,7 +483,7 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
       }
       fence_proxy_async_smem();
       mbar_arrive(smem_u32(&sm.empty[stage]));
-      if (++stage == kSkStages) { stage = 0; phase ^= 1; }
+      if (++stage == ST) { stage = 0; phase ^= 1; }
     }
     if (ok && mbar_wait(smem_u32(&sm.tfull), 0, abort, kSiteSkTfull)) {
       tc_fence_after();
@@ -538,6 +546,190 @@ k1_fwd_tc_splitk_kernel(const __grid_constant__ CUtensorMap tmap_x,
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem, 32);
+  }
+}
+
+// ---------------------------------------------------------------------------
+// K1 forward for very few tokens, split over a thread-block cluster.
+//
+// With T <= 2 x (SMs / 2) tokens the one-block-per-2-tokens CUDA-core kernel
+// (k1_simt.cu) leaves most SMs idle and each block walks all of W (nC x 32
+// bf16) itself.  Here the 2-token pair gets a cluster of S CTAs (S = 8, 4 or
+// 2, the largest that keeps the grid within one wave); CTA r of the cluster
+// takes the 16-byte chunks [r nch / S, (r + 1) nch / S) of the row.  Inside a
+// CTA the four warp pairs split W's 32 rows into groups of 8 (warps 2g, 2g+1
+// take rows 8g .. 8g+7) and the 64 threads of a pair walk the chunks, so a
+// thread issues its x load and 8 W loads in one batch.  Per value a warp
+// butterfly, then the two warps of a group are added in warp order; the
+// CTA's 66 partials (2 tokens x (32 projections + sum of squares)) go to rank 0
+// through distributed shared memory (st.shared::cluster, then an arrive with
+// release at cluster scope on rank 0's mbarrier), and rank 0 adds them in
+// rank order after a bounded wait.  Rank 0 then writes proj and inv_rms and,
+// as k1_fwd_rows_kernel, runs K2 (COEFFS) and K3 (PRE) for its tokens.  The
+// other ranks exit after sending; rank 0 never touches their memory.  Only the
+// barrier set-up uses the cluster-wide hardware barrier.  Same preconditions
+// as the CUDA-core small-T kernel: D == 32, nC % 8 == 0, x and W 16-byte
+// aligned (PRE: nC % 32 == 0 and 16-byte aligned pre_out).
+constexpr int kRcTokens = 2;
+constexpr int kRcThreads = 256;
+constexpr int kRcMaxS = 8;
+constexpr int kRcVals = kRcTokens * 33;
+enum : unsigned { kSiteRcRecv = 0x121 };
+
+template <bool COEFFS, bool PRE>
+__global__ void __launch_bounds__(kRcThreads, 1)
+k1_fwd_rows_cluster_kernel(const __nv_bfloat16 *__restrict__ x, const __nv_bfloat16 *__restrict__ W,
+                           __nv_bfloat16 *__restrict__ out, float *__restrict__ inv_rms, int64_t T,
+                           int nC, int S, const K2Params P, const k2tok::Out co,
+                           __nv_bfloat16 *__restrict__ pre_out) {
+  static_assert(COEFFS || !PRE, "K3 needs the coefficients");
+  __shared__ float red[8][kRcTokens][9];
+  __shared__ float recv[kRcMaxS][kRcVals];  // rank 0: slot r holds rank r's partials
+  __shared__ float tot[kRcTokens][33];
+  __shared__ alignas(8) uint64_t rfull;
+  __shared__ k2tok::ParamSmem k2s;
+  __shared__ float4 hs[kRcTokens];
+  __shared__ int abort_flag;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const uint32_t rank = cluster_ctarank();
+  if (tid == 0) {
+    if (rank == 0) mbar_init(smem_u32(&rfull), uint32_t(S - 1) * kRcVals);
+    abort_flag = 0;
+    fence_mbar_init();
+  }
+  __syncthreads();
+  // rank 0's barrier exists before any peer arrives on it
+  cluster_sync_all();
+  // No global memory is touched before this point (see pdl_wait()).
+  pdl_wait();
+  if (COEFFS && rank == 0) k2tok::stage_params(k2s, P, tid, kRcThreads);
+
+  const int64_t t0 = int64_t(blockIdx.x / S) * kRcTokens;
+  const bool has1 = t0 + 1 < T;
+  const int nch = nC >> 3;
+  const int c0 = int(rank) * nch / S, c1 = (int(rank) + 1) * nch / S;
+  const int g = warp >> 1;    // W rows 8g .. 8g+7
+  const int j = tid & 63;     // thread within the warp pair
+  float acc0[8], acc1[8], ss0 = 0.f, ss1 = 0.f;
+#pragma unroll
+  for (int i = 0; i < 8; ++i) acc0[i] = acc1[i] = 0.f;
+  for (int c = c0 + j; c < c1; c += 64) {
+    const uint4 u0 = __ldg(reinterpret_cast<const uint4 *>(x + t0 * nC + c * 8));
+    uint4 u1 = make_uint4(0u, 0u, 0u, 0u);
+    if (has1) u1 = __ldg(reinterpret_cast<const uint4 *>(x + (t0 + 1) * nC + c * 8));
+    uint4 wv[8];
+#pragma unroll
+    for (int i = 0; i < 8; ++i)
+      wv[i] = __ldg(reinterpret_cast<const uint4 *>(W + int64_t(8 * g + i) * nC + c * 8));
+    const float f0[8] = {bf16lo(u0.x), bf16hi(u0.x), bf16lo(u0.y), bf16hi(u0.y),
+                         bf16lo(u0.z), bf16hi(u0.z), bf16lo(u0.w), bf16hi(u0.w)};
+    const float f1[8] = {bf16lo(u1.x), bf16hi(u1.x), bf16lo(u1.y), bf16hi(u1.y),
+                         bf16lo(u1.z), bf16hi(u1.z), bf16lo(u1.w), bf16hi(u1.w)};
+#pragma unroll
+    for (int e = 0; e < 8; ++e) {
+      ss0 = fmaf(f0[e], f0[e], ss0);
+      ss1 = fmaf(f1[e], f1[e], ss1);
+    }
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      const uint4 u = wv[i];
+      const float fw[8] = {bf16lo(u.x), bf16hi(u.x), bf16lo(u.y), bf16hi(u.y),
+                           bf16lo(u.z), bf16hi(u.z), bf16lo(u.w), bf16hi(u.w)};
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        acc0[i] = fmaf(f0[e], fw[e], acc0[i]);
+        acc1[i] = fmaf(f1[e], fw[e], acc1[i]);
+      }
+    }
+  }
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int off = 16; off >= 1; off >>= 1) {
+      acc0[i] += __shfl_xor_sync(0xffffffffu, acc0[i], off);
+      acc1[i] += __shfl_xor_sync(0xffffffffu, acc1[i], off);
+    }
+#pragma unroll
+  for (int off = 16; off >= 1; off >>= 1) {
+    ss0 += __shfl_xor_sync(0xffffffffu, ss0, off);
+    ss1 += __shfl_xor_sync(0xffffffffu, ss1, off);
+  }
+  if (lane == 0) {
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      red[warp][0][i] = acc0[i];
+      red[warp][1][i] = acc1[i];
+    }
+    red[warp][0][8] = ss0;  // every group sums the squares; group 0's are used
+    red[warp][1][8] = ss1;
+  }
+  __syncthreads();
+  if (tid < kRcVals) {
+    const int tb = tid / 33, d = tid - tb * 33;
+    const int gg = d < 32 ? d >> 3 : 0, i = d < 32 ? d & 7 : 8;
+    const float v = red[2 * gg][tb][i] + red[2 * gg + 1][tb][i];
+    if (rank != 0) {
+      st_cluster_f32(mapa_shared(smem_u32(&recv[rank][tid]), 0), v);
+      mbar_arrive_remote(mapa_shared(smem_u32(&rfull), 0));
+    } else {
+      recv[0][tid] = v;
+    }
+  }
+  if (rank != 0) return;
+  __syncthreads();
+  if (tid < kRcVals) {
+    if (S == 1 || mbar_wait_cluster(smem_u32(&rfull), 0, &abort_flag, kSiteRcRecv)) {
+      float v = recv[0][tid];
+      for (int r = 1; r < S; ++r) v += recv[r][tid];
+      tot[tid / 33][tid % 33] = v;
+    }
+  }
+  __syncthreads();
+  if (abort_flag) return;
+  if (tid < kRcTokens * 32) {
+    const int tb = tid / 32, d = tid - tb * 32;
+    const int64_t t = t0 + tb;
+    if (t < T) {
+      const float r = rsqrtf(tot[tb][32] / float(nC) + kEps);
+      out[t * 32 + d] = __float2bfloat16_rn(tot[tb][d] * r);
+      if (d == 0) inv_rms[t] = r;
+    }
+  }
+  if constexpr (COEFFS) {
+    if (tid < kRcTokens && t0 + tid < T) {
+      const int64_t t = t0 + tid;
+      const float r = rsqrtf(tot[tid][32] / float(nC) + kEps);
+      float pv[32];  // the logits as stored above (bf16)
+#pragma unroll
+      for (int d = 0; d < 32; ++d) pv[d] = __bfloat162float(__float2bfloat16_rn(tot[tid][d] * r));
+      hs[tid] = k2tok::store_coeffs(k2s, pv, co.h_pre, co.h_post, co.H, t);
+    }
+  }
+  if constexpr (PRE) {
+    __syncthreads();
+    const int C = nC >> 2, n3 = C >> 3;
+    for (int it = tid; it < kRcTokens * n3; it += kRcThreads) {
+      const int tb = it / n3, c = it - tb * n3;
+      const int64_t t = t0 + tb;
+      if (t >= T) continue;
+      const float4 h = hs[tb];
+      const __nv_bfloat16 *xr = x + t * nC;
+      Chunk<8> a0, a1, a2, a3;
+      a0.v = __ldg(reinterpret_cast<const uint4 *>(xr + c * 8));
+      a1.v = __ldg(reinterpret_cast<const uint4 *>(xr + C + c * 8));
+      a2.v = __ldg(reinterpret_cast<const uint4 *>(xr + 2 * C + c * 8));
+      a3.v = __ldg(reinterpret_cast<const uint4 *>(xr + 3 * C + c * 8));
+      float f0[8], f1[8], f2[8], f3[8], o[8];
+      unpack(a0, f0); unpack(a1, f1); unpack(a2, f2); unpack(a3, f3);
+#pragma unroll
+      for (int e = 0; e < 8; ++e) {
+        float acc = h.x * f0[e];
+        acc = fmaf(h.y, f1[e], acc);
+        acc = fmaf(h.z, f2[e], acc);
+        o[e] = fmaf(h.w, f3[e], acc);
+      }
+      store_stream<8>(pre_out + t * C + c * 8, o);
+    }
   }
 }
 
@@ -636,8 +828,41 @@ const char *k1_tc_error() { return k1tc::g_msg; }
 static_assert(sizeof(k1tc::BwdSmem) + 1024 <= 232448, "K1 backward shared memory");
 static_assert((sizeof(k1tc::FwdSmem) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
               "K1 forward shared memory");
-static_assert((sizeof(k1tc::SkSmem) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
+static_assert((sizeof(k1tc::SkSmem<k1tc::kSkStagesShallow>) + 1024) * FMHC_K1F_CTAS_PER_SM <= 232448,
               "split-K K1 forward shared memory");
+static_assert(sizeof(k1tc::SkSmem<k1tc::kSkStagesDeep>) + 1024 <= 232448,
+              "split-K K1 forward shared memory (one CTA per SM)");
+
+int launch_k1_fwd_rows_cluster(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
+                               int nC, cudaStream_t s, const K2Params *coeffs, float *h_pre,
+                               float *h_post, float *H, void *pre_out) {
+  using namespace k1tc;
+#ifndef FMHC_K1F_ROWS_CLUSTER  // 0 keeps the one-block-per-2-tokens kernel (A/B measurements)
+#define FMHC_K1F_ROWS_CLUSTER 1
+#endif
+  if (!FMHC_K1F_ROWS_CLUSTER || T < 1 || !device_is_sm100()) return -1;
+  const int64_t pairs = (T + kRcTokens - 1) / kRcTokens;
+  const int64_t sms = device_sms();
+  int S = 0;
+  for (int c : {8, 4, 2})
+    if (pairs * c <= sms) { S = c; break; }
+  if (S == 0) return -1;
+  const K2Params P = coeffs ? *coeffs : K2Params{};
+  const k2tok::Out co{reinterpret_cast<float4 *>(h_pre), reinterpret_cast<float4 *>(h_post),
+                      reinterpret_cast<float4 *>(H)};
+  auto kern = !coeffs ? k1_fwd_rows_cluster_kernel<false, false>
+            : pre_out ? k1_fwd_rows_cluster_kernel<true, true>
+                      : k1_fwd_rows_cluster_kernel<true, false>;
+  if (launch_cluster(kern, dim3(unsigned(pairs * S)), dim3(kRcThreads), 0, s, unsigned(S),
+                     reinterpret_cast<const __nv_bfloat16 *>(x),
+                     reinterpret_cast<const __nv_bfloat16 *>(W),
+                     reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, S, P, co,
+                     reinterpret_cast<__nv_bfloat16 *>(pre_out)) != cudaSuccess) {
+    snprintf(g_msg, sizeof(g_msg), "cluster launch of the small-T K1 forward failed");
+    return 4;
+  }
+  return 0;
+}
 
 bool k1_tc_fwd_supported(const void *x, const void *W, const void *out, const float *inv_rms,
                          int64_t T, int64_t nC, int64_t D) {
@@ -670,6 +895,9 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
 #ifndef FMHC_K1F_SPLITK  // 0 disables the split-K path (A/B measurements)
 #define FMHC_K1F_SPLITK 1
 #endif
+#ifndef FMHC_K1F_SK_DEEP  // 0 keeps the shallow pipeline everywhere (A/B measurements)
+#define FMHC_K1F_SK_DEEP 1
+#endif
     if (FMHC_K1F_SPLITK && tiles * 4 <= sms && nk >= 8) S = 4;
     else if (FMHC_K1F_SPLITK && tiles * 2 * 4 <= slots * 3 && nk >= 4) S = 2;
     if (S) {
@@ -681,8 +909,13 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
         snprintf(g_msg, sizeof(g_msg), "cuTensorMapEncodeTiled failed");
         return 5;
       }
-      const size_t smem = sizeof(SkSmem) + 1024;
-      auto kern = coeffs ? k1_fwd_tc_splitk_kernel<true> : k1_fwd_tc_splitk_kernel<false>;
+      // One CTA per SM when the clusters fit: the deep pipeline.
+      const bool deep = tiles * S <= sms && FMHC_K1F_SK_DEEP;
+      const size_t smem = (deep ? sizeof(SkSmem<kSkStagesDeep>) : sizeof(SkSmem<kSkStagesShallow>)) + 1024;
+      auto kern = deep ? (coeffs ? k1_fwd_tc_splitk_kernel<true, kSkStagesDeep>
+                                 : k1_fwd_tc_splitk_kernel<false, kSkStagesDeep>)
+                       : (coeffs ? k1_fwd_tc_splitk_kernel<true, kSkStagesShallow>
+                                 : k1_fwd_tc_splitk_kernel<false, kSkStagesShallow>);
       if (int e = set_smem_attr(reinterpret_cast<const void *>(kern), smem)) return e;
       if (launch_cluster(kern, dim3(unsigned(tiles * S)), dim3(kThreads), smem, s, unsigned(S), mx,
                          mw, reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, S, P,

@@ -20,6 +20,15 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
                      float *h_post = nullptr, float *H = nullptr);
 const char *k1_tc_error();
 
+// K1 forward for T <= 2 x (SMs / 2) tokens on the CUDA cores, each 2-token
+// pair split over a cluster of 2-8 CTAs (same preconditions and options as
+// launch_k1_fwd_rows).  Returns 0 when launched, -1 when T is too large for
+// it (the caller then runs launch_k1_fwd_rows), or an fmhc_status code.
+int launch_k1_fwd_rows_cluster(const void *x, const void *W, void *out, float *inv_rms, int64_t T,
+                               int nC, cudaStream_t s, const K2Params *coeffs = nullptr,
+                               float *h_pre = nullptr, float *h_post = nullptr, float *H = nullptr,
+                               void *pre_out = nullptr);
+
 // Backward (grad_x, and grad_W when gW != nullptr) on the tensor cores.
 bool k1_tc_bwd_supported(const void *go, const void *x, const void *W, const void *proj,
                          const void *gx, int64_t T, int64_t nC, int64_t D);

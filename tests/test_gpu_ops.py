@@ -245,6 +245,20 @@ def _kernel_names(fn):
     return {e.name for e in prof.events() if e.device_type == torch.autograd.DeviceType.CUDA}
 
 
+@pytest.mark.parametrize("T,kernel", [(1, "k1_fwd_rows_cluster_kernel"),
+                                      (148, "k1_fwd_rows_cluster_kernel"),
+                                      (150, "k1_fwd_rows_kernel"),
+                                      (4096, "k1_fwd_tc_splitk_kernel")])
+def test_small_t_k1_forward_kernel_choice(T, kernel):
+    """Few tokens: clusters of CTAs per token pair while the pairs are too few to
+    fill the GPU, then one block per pair, then the split-K tensor-core kernel."""
+    xf = torch.randn(T, 3072, device="cuda").bfloat16()
+    W = (torch.randn(32, 3072, device="cuda") * 0.02).bfloat16()
+    names = _kernel_names(lambda: torch.ops.flash_mhc.fused_rmsnorm_project(xf, W))
+    assert any(kernel in n and (kernel != "k1_fwd_rows_kernel" or "cluster" not in n)
+               for n in names), names
+
+
 def test_metric_shape_runs_the_tensor_core_k1():
     """At T=65536, nC=4096 the K1 forward and backward are the TMA + tcgen05 kernels."""
     d = _inputs(256, 1024, 9)
@@ -259,13 +273,16 @@ def test_metric_shape_runs_the_tensor_core_k1():
     assert any("k1_bwd_tc_kernel" in n for n in names), names
 
 
-@pytest.mark.parametrize("T,C", [(1, 256), (31, 256), (33, 256), (1000, 256), (4733, 256),
+@pytest.mark.parametrize("T,C", [(1, 256), (31, 256), (33, 256), (60, 256), (148, 256),
+                                 (150, 256), (1000, 256), (4733, 256),
                                  (3000, 1024), (129, 2048),
                                  (65536, 64),   # 2 k-chunks: 74 CTAs add into each
                                  (20000, 1024),  # groups of 4 k-chunks, 18 or 19 CTAs each
                                  (6000, 768)])  # groups of 2, 12 or 13 CTAs each, nC = 3072
 def test_k1_token_partitioning(T, C):
-    """Forward: token ranges split across CTAs in 32-row units, partial tiles.
+    """Forward: token pairs split over clusters of 8, 4 and 2 CTAs (T = 1 .. 148),
+    one block per pair (150), token ranges split across CTAs in 32-row units,
+    partial tiles.
     Backward: the k-chunks form groups of G (1, 2, 4 or 8, chosen per shape),
     each CTA of a group takes every ng-th token tile; groups of unequal CTA
     counts, fewer tiles than CTAs, partial token tiles; grad_W reduction."""

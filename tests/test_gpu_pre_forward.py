@@ -37,13 +37,14 @@ def _inputs(T, C, pdtype, seed):
     return x, W, a, bias, perm
 
 
-# (T, C): row kernel with K3 inside (C % 8 == 0) and with K3 separate
-# (C = 20, 36), split-K S = 4 (T = 889, 4096) and S = 2 (8192), the
+# (T, C): the small-T kernels -- token pairs over clusters of 8, 4 or 2 CTAs
+# (T <= 148) and one block per pair -- with K3 inside (C % 8 == 0) and with K3
+# separate (C = 20, 36), split-K S = 4 (T = 889, 4096) and S = 2 (8192), the
 # persistent tensor-core kernel (20000; 65537 with a tail tile), the CUDA-core
 # kernel (nC = 80 is no multiple of the tensor-core k-step).
-SHAPES = [(1, 768), (2, 768), (3, 1024), (16, 768), (256, 768), (888, 1024), (5, 20),
-          (300, 36), (889, 1024), (4096, 1024), (8192, 768), (20000, 768), (65537, 1024),
-          (1000, 20)]
+SHAPES = [(1, 768), (2, 768), (3, 1024), (16, 768), (60, 768), (148, 64), (149, 768),
+          (256, 768), (888, 1024), (5, 20), (300, 36), (889, 1024), (4096, 1024), (8192, 768),
+          (20000, 768), (65537, 1024), (1000, 20)]
 
 
 @pytest.mark.parametrize("pdtype", [torch.float32, torch.bfloat16])
