@@ -58,6 +58,42 @@ def test_fake_impls_match_reference_shapes_and_dtypes():
         assert gx.shape == xf.shape and gW.shape == W.shape and gW.dtype == torch.bfloat16
 
 
+def test_fake_impls_of_added_ops():
+    """The ops this build adds (K2, the fused pre-block forward and the pieces
+    of the block backward) have fake implementations with the CUDA impls'
+    output shapes and dtypes, so they trace under torch.compile."""
+    from torch._subclasses.fake_tensor import FakeTensorMode
+
+    ops = torch.ops.flash_mhc
+    T, n, C = 8, 4, 16
+    shp = lambda ts: [(tuple(t.shape), t.dtype) for t in (ts if isinstance(ts, tuple) else (ts,))]  # noqa: E731
+    bf, f32 = torch.bfloat16, torch.float32
+    with FakeTensorMode():
+        x = torch.empty(T, n, C, dtype=bf)
+        W = torch.empty(32, n * C, dtype=bf)
+        proj = torch.empty(T, 32, dtype=bf)
+        h = torch.empty(T, n, dtype=f32)
+        H = torch.empty(T, n, n, dtype=f32)
+        lo = torch.empty(T, C, dtype=bf)
+        a = torch.empty(1, dtype=bf)
+        bias = torch.empty(32, dtype=bf)
+        perm = torch.empty(24, 16, dtype=f32)
+        assert shp(ops.mhc_pre_forward(x, W, a, a, a, bias, perm)) == [
+            ((T, C), bf), ((T, 32), bf), ((T,), f32), ((T, 4), f32), ((T, 4), f32),
+            ((T, 4, 4), f32)]
+        assert shp(ops.mhc_coeffs(proj, a, a, a, bias, perm)) == [
+            ((T, 4), f32), ((T, 4), f32), ((T, 4, 4), f32)]
+        assert shp(ops.mhc_coeffs_backward_split(h, h, H, proj, a, a, a, bias, perm)) == [
+            ((T, 32), bf), ((1,), bf), ((1,), bf), ((1,), bf), ((32,), bf)]
+        assert shp(ops.mhc_coeffs_backward(h, h, H, proj, a, a, a, bias, perm)) == [
+            ((T, 32), bf), ((35,), f32)]
+        assert shp(ops.pre_map_grad_h(lo, x, h)) == [((T, n), f32)]
+        assert shp(ops.post_res_grad_params(x, x, lo, H, h)) == [
+            ((T, C), bf), ((T, n, n), f32), ((T, n), f32)]
+        assert shp(ops.mhc_grad_x_combine(x, lo, h, None)) == [((T, n, C), bf)]
+        assert shp(ops.mhc_grad_x_combine_post(x, lo, h, x, H)) == [((T, n, C), bf)]
+
+
 def test_ops_raise_on_cpu_tensors_like_reference():
     """No CPU kernel is registered (reference behaviour): CPU tensors raise."""
     x = torch.zeros(4, 4, 8, dtype=torch.bfloat16)
