@@ -406,7 +406,9 @@ def run_tiny_inference(args, torch, dev):
     (T in {1, 16, 256}, C = 768, n = 4 bf16, x ~N(0,1)
     with 1% of channels x100, projection weights ~N(0,0.02), wrapped
     768 -> 768 bias-free linear), eager and replayed from a CUDA graph.
-    Microseconds per forward, averaged over 200 back-to-back calls."""
+    Microseconds per forward, averaged over 200 back-to-back calls; with one
+    forward per graph replay (graph_us) and with 20 forwards captured in one
+    graph (graph_x20_us, per forward)."""
     import torch.nn as nn
 
     from flash_mhc import MHCLiteBlock
@@ -456,7 +458,16 @@ def run_tiny_inference(args, torch, dev):
             fwd()
         graph_us = timed(graph.replay)
         del graph
-        out[str(T)] = {"eager_us": round(eager_us, 2), "graph_us": round(graph_us, 2)}
+        # 20 forwards in one graph: the device time of a forward without the
+        # per-replay launch of the graph itself
+        graph20 = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(graph20):
+            for _ in range(20):
+                fwd()
+        graph20_us = timed(graph20.replay) / 20
+        del graph20
+        out[str(T)] = {"eager_us": round(eager_us, 2), "graph_us": round(graph_us, 2),
+                       "graph_x20_us": round(graph20_us, 2)}
     return {"config": {"workload": "MHCLiteBlock no-grad forward (configs[4] tiny-T shapes)",
                        "C": C, "n": N_STREAMS, "layer": "nn.Linear(768, 768, bias=False)",
                        "x": "N(0,1), 1% of channels x100"},
