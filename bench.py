@@ -26,12 +26,16 @@ all-reduced over NCCL, the path's only exchange.
   bandwidth in MEASURED_PEAKS.json.
 * ``e2e``: the same step from pinned host buffers, host->device copies of every
   input and device->host copies of every output inside the timed region.
-* ``cpu_baseline``: the CPU restatement (oracle/, float32 numpy, one process
-  per core) on a bounded token sample, rank 0 only.
-* ``--impl reference``: the reference arm.  The reference's kernels are
-  Triton-only and it has no compiled CPU implementation of this path, so the
-  arm times the CPU restatement of the reference algorithm (oracle port) with
-  all host cores on the same workload, rank 0 only.
+* ``cpu_baseline``: the reference's own CPU implementation of the path (its
+  pure-PyTorch block code from the unmodified reference installed in
+  ``baseline/_ref``, float32, every host core) on a bounded token sample,
+  rank 0 at N = 1 only, run in a child process; ``configs0`` inside it is
+  BASELINE configs[0] (the reference's ``MHCLiteBlock`` fwd+bwd on CPU at
+  T=4096, C=1024).
+* ``--impl reference``: the reference arm: the same reference code on the
+  full per-GPU batch (T tokens) per step, rank 0 only.  Where
+  ``baseline/_ref`` is missing it falls back to the float32 numpy
+  restatement under ``oracle/`` (``kind: "port"``).
 * ``--impl reference-triton``: a comparison line, not the reference arm -- the
   unmodified reference's Triton kernels and block, installed in
   ``baseline/_ref``, timed on this GPU on the same shapes and seeds.
@@ -196,8 +200,9 @@ class HotPath:
             "g_post": rn(T, n, C),
         }
 
-    def step(self, inp, events=None):
-        """One pass; ``events`` (dict name -> list) gets (start, end) event pairs."""
+    def step(self, inp, events=None, after_k4_fwd=None):
+        """One pass; ``events`` (dict name -> list) gets (start, end) event pairs;
+        ``after_k4_fwd`` is called once K4's forward is enqueued."""
         torch = self.torch
         ops = torch.ops.flash_mhc
         T, C = self.T, self.C
@@ -219,6 +224,8 @@ class HotPath:
         outs["proj"], outs["inv_rms"] = rec("k1_fwd", lambda: ops.fused_rmsnorm_project(xf, inp["W"]))
         outs["layer_input"] = rec("k3_fwd", lambda: ops.fused_pre_map(x, inp["h_pre"]))
         outs["out"] = rec("k4_fwd", lambda: ops.fused_post_res(x, inp["lo"], inp["H"], inp["h_post"]))
+        if after_k4_fwd is not None:
+            after_k4_fwd()
         (outs["gx4"], outs["glo"], outs["gH"], outs["ghp"]) = rec(
             "k4_bwd", lambda: ops.fused_post_res_backward(inp["g_post"], x, inp["lo"], inp["H"],
                                                           inp["h_post"]))
@@ -239,6 +246,45 @@ def _allreduce_gw(torch, dist, outs):
     return buf
 
 
+def _stepper(hp, torch, dist, world):
+    """(one_step, join_comm) for the hot path on ``world`` ranks.
+
+    With N > 1 the weight-gradient all-reduce of step i (the path's only
+    exchange; nothing in step i+1 reads grad_W) is issued on a side stream
+    during step i+1, ordered after that step's K4 forward, so NCCL's kernel runs
+    beside the streaming K4/K3 backward instead of competing for SMs and L2
+    with the persistent K1 forward that starts the step.  ``join_comm`` issues
+    the last step's all-reduce and makes the current stream wait for it; every
+    timed region ends with it.
+    """
+    if world == 1:
+        return (lambda events=None: hp.step(hp.inputs, events)), (lambda: None)
+    s_comm = torch.cuda.Stream()
+    pending = []  # the previous step's outputs, their grad_W not reduced yet
+
+    def launch_pending():
+        if not pending:
+            return
+        prev = pending.pop()
+        ready = torch.cuda.Event()
+        ready.record()
+        s_comm.wait_event(ready)
+        with torch.cuda.stream(s_comm):
+            prev["gW_all"] = _allreduce_gw(torch, dist, prev)
+            prev["gW"].record_stream(s_comm)
+
+    def one_step(events=None):
+        outs = hp.step(hp.inputs, events, after_k4_fwd=launch_pending)
+        pending.append(outs)
+        return outs
+
+    def join_comm():
+        launch_pending()
+        torch.cuda.current_stream().wait_stream(s_comm)
+
+    return one_step, join_comm
+
+
 def run_ours(args):
     import torch
     import torch.distributed as dist
@@ -255,31 +301,18 @@ def run_ours(args):
     dev = torch.device("cuda", local)
     if world > 1:
         from datetime import timedelta
-        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev)
+        opts = dist.ProcessGroupNCCL.Options()
+        if args.nccl_max_ctas > 0:
+            opts.config.max_ctas = args.nccl_max_ctas
+        if args.nccl_nvls_ctas > 0:
+            opts.config.nvls_ctas = args.nccl_nvls_ctas
+        dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev,
+                                pg_options=opts)
 
     T, C = args.T, args.C
     hp = HotPath(T, C, dev, seed=1234 + rank, torch=torch)
     lib_path = str(_native.library_path())
-
-    # With N > 1 the weight-gradient all-reduce of step i runs on a side stream
-    # while step i+1's kernels run (nothing in the next step reads grad_W); the
-    # timed regions end only after the last all-reduce (join_comm()).
-    s_comm = torch.cuda.Stream() if world > 1 else None
-
-    def one_step(events=None):
-        outs = hp.step(hp.inputs, events)
-        if world > 1:
-            ready = torch.cuda.Event()
-            ready.record()
-            s_comm.wait_event(ready)
-            with torch.cuda.stream(s_comm):
-                outs["gW_all"] = _allreduce_gw(torch, dist, outs)
-                outs["gW"].record_stream(s_comm)
-        return outs
-
-    def join_comm():
-        if world > 1:
-            torch.cuda.current_stream().wait_stream(s_comm)
+    one_step, join_comm = _stepper(hp, torch, dist, world)
 
     # --- device-resident timing -------------------------------------------
     for _ in range(args.warmup):
@@ -330,6 +363,9 @@ def run_ours(args):
     # --- the whole block ------------------------------
     block = None if args.no_block else run_block(args, torch, dist, world, dev)
 
+    # --- the large token-sharded config ---------------
+    large = None if args.no_large else run_large(args, torch, dist, world, dev)
+
     # --- small per-GPU batch: eager vs CUDA-graph replay -------------------
     graphs = None if args.no_graphs else run_small_graphs(args, torch, dev)
 
@@ -340,17 +376,21 @@ def run_ours(args):
         peaks = measured_peaks()
         bm = bytes_model(T, C)
         traffic = dram_traffic()
+        def traffic_of(k):
+            # ncu DRAM bytes per launch, scaled from a small capture; they apply
+            # only to the (T, C) they were scaled to
+            cap = traffic.get(k, {}) if traffic else {}
+            return (cap.get("bytes_per_launch_full")
+                    if cap.get("full_T") == T and cap.get("C", C) == C else None)
+
         kernels = {}
         for k, v in kern_ms.items():
             gbs = bm[k] / (v * 1e-3) / 1e9
             kernels[k] = {"ms": round(v, 5), "bytes": bm[k], "GBps": round(gbs, 1),
-                          "frac": round(gbs / peaks["hbm_gbs"], 4)}
+                          "frac": round(gbs / peaks["hbm_gbs"], 4), "traffic": traffic_of(k)}
         dom = "k4_bwd"
         ach = bm[dom] / (kern_ms[dom] * 1e-3) / 1e9
-        # ncu traffic applies only to the (T, C) it was scaled to
-        cap = traffic.get(dom, {}) if traffic else {}
-        tr = (cap.get("bytes_per_launch_full")
-              if cap.get("full_T") == T and cap.get("C", C) == C else None)
+        tr = traffic_of(dom)
         sum_bytes = sum(bm.values())
         line = {
             "metric": METRIC, "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT,
@@ -358,15 +398,14 @@ def run_ours(args):
             "ms_per_step": round(ms, 5), "higher_is_better": True, "scaling": "weak",
             "vs_baseline": None, "dtype": "bf16",
             "data": "synthetic (seeded N(0,1) x/lo/grads, N(0,0.02) W, N(0,1) f32 coefficients)",
-            "config": {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
-                       "T_per_gpu": T, "C": C, "n": N_STREAMS, "D": D_OUT,
-                       "step": "K1f,K3f,K4f,K4b,K3b,K1b(dx+dW)" + (",allreduce(gW)" if world > 1 else ""),
-                       "parallelism": f"token-sharded dp{world}",
-                       "l2": f"inputs larger than L2 (x alone {T * N_STREAMS * C * 2 / 2**20:.0f} MiB), "
-                             "no flush",
-                       "timing": "value: steps timed with events at the region's ends only; "
-                                 "kernels/roofline: a second region of the same steps with an "
-                                 "event pair around every op"},
+            "config": workload_config(T, C, world),
+            "timing": "value: steps timed with events at the region's ends only; "
+                      "kernels/roofline: a second region of the same steps with an "
+                      "event pair around every op",
+            # BASELINE's metric name says "per GPU"; `value` is the whole-job
+            # figure the bench contract asks for, and this is the per-GPU one.
+            "value_scope": "whole job: tokens/s over all n_gpus GPUs",
+            "per_gpu": {"value": round(T / (ms * 1e-3), 1), "unit": "tokens/s per GPU"},
             "roofline": {"kernel": dom, "bound": "hbm", "achieved": round(ach, 1),
                          "peak": peaks["hbm_gbs"], "peak_src": peaks["src"], "unit": "GB/s",
                          "frac": round(ach / peaks["hbm_gbs"], 4),
@@ -376,6 +415,7 @@ def run_ours(args):
             "kernels": kernels,
             "e2e": e2e,
             "block": block,
+            "large": large,
             "small_batch_graphs": graphs,
             "tiny_inference": tiny,
             "gpu_launches": HotPath.LAUNCHES_PER_STEP * args.steps,
@@ -513,17 +553,21 @@ def run_small_graphs(args, torch, dev):
             "graph_tokens_per_s": round(T / (graph_ms * 1e-3), 1)}
 
 
-def run_block(args, torch, dist, world, dev):
+def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
     """MHCLiteBlock fwd+bwd with activation checkpointing:
     T tokens per GPU, C=2048, n=4 bf16, wrapped nn.Linear(C, C, bias=False)
-    ~N(0,0.02), upstream grad ~N(0,1); with N GPUs the block's parameter
-    gradients are all-reduced (one bucket) every step."""
+    ~N(0,0.02), upstream grad ~N(0,1).  With N GPUs every parameter gradient
+    is all-reduced each step by ``BucketedGradReducer``: the layer's gradient
+    starts reducing as soon as the layer's backward has produced it, while the
+    block's K3/K2/K1 backward and grad_x combination still run; the block's
+    own gradients follow at the end."""
     import torch.nn as nn
 
     from flash_mhc import MHCLiteBlock
-    from flash_mhc.distributed import allreduce_gradients
+    from flash_mhc.distributed import BucketedGradReducer
 
-    T, C = args.block_T, args.block_C
+    T = T or args.block_T
+    C = C or args.block_C
     g = torch.Generator(device=dev)
     g.manual_seed(77)
     layer = nn.Linear(C, C, bias=False)
@@ -533,14 +577,15 @@ def run_block(args, torch, dist, world, dev):
         layer.weight.copy_((torch.randn(C, C, generator=g, device=dev) * 0.02).bfloat16())
     x = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16().requires_grad_(True)
     up = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16()
+    reducer = BucketedGradReducer(blk) if world > 1 else None
 
     def step():
         blk.zero_grad(set_to_none=True)
         x.grad = None
         out = blk(x)
         out.backward(up)
-        if world > 1:
-            allreduce_gradients(blk)
+        if reducer is not None:
+            reducer.finish()
 
     steps = max(1, min(args.steps, 10))
     for _ in range(max(3, min(args.warmup, 5))):
@@ -560,12 +605,67 @@ def run_block(args, torch, dist, world, dev):
         tt = torch.tensor([ms], device=dev)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
+    if reducer is not None:
+        reducer.remove()
     flops = 3 * 2 * T * C * C  # the wrapped layer's fwd + 2 bwd GEMMs
-    return {"config": {"workload": "MHCLiteBlock fwd+bwd, activation checkpointing (configs[2])",
+    return {"config": {"workload": workload or "MHCLiteBlock fwd+bwd, activation checkpointing "
+                                               "(configs[2])",
                        "T_per_gpu": T, "C": C, "n": N_STREAMS,
-                       "layer": "nn.Linear(C, C, bias=False) ~N(0,0.02)"},
+                       "layer": f"nn.Linear({C}, {C}, bias=False) ~N(0,0.02)",
+                       "grad_allreduce": "bucketed, overlapped with the backward" if world > 1
+                       else "none (1 GPU)"},
             "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT, "ms_per_step": round(ms, 4),
             "steps": steps, "layer_gemm_tflops_per_step": round(flops / 1e12, 3)}
+
+
+def run_large(args, torch, dist, world, dev):
+    """BASELINE configs[3], the large token-sharded run, per GPU: 131,072
+    tokens per GPU (global T = 131,072 x N; 1,048,576 on 8 GPUs), C = 4096,
+    n = 4 bf16.  (1) The hot-path step (same six ops and the grad_W all-reduce
+    as the headline, 2 MiB of f32 per step); (2) the MHCLiteBlock fwd+bwd with
+    the wrapped 4096 -> 4096 bias-free linear, whose 64 MiB f32 gradient is
+    all-reduced with the block's own.  Weak scaling: the per-GPU work is fixed.
+    Each (T, 4, C) bf16 tensor holds 4 GiB."""
+    T, C = args.large_T, args.large_C
+    hp = HotPath(T, C, dev, seed=4321 + int(os.environ.get("RANK", "0")), torch=torch)
+    one_step, join_comm = _stepper(hp, torch, dist, world)
+    steps = max(1, min(args.steps, 10))
+    for _ in range(3):
+        one_step()
+    join_comm()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    s = torch.cuda.Event(enable_timing=True)
+    e = torch.cuda.Event(enable_timing=True)
+    s.record()
+    for _ in range(steps):
+        one_step()
+    join_comm()
+    e.record()
+    torch.cuda.synchronize()
+    ms = s.elapsed_time(e) / steps
+    if world > 1:
+        tt = torch.tensor([ms], device=dev)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        ms = float(tt.item())
+    del hp, one_step, join_comm
+    torch.cuda.empty_cache()
+    bm = sum(bytes_model(T, C).values())
+    peaks = measured_peaks()
+    out = {"config": {"workload": "large token-sharded hot path fwd+bwd (configs[3])",
+                      "T_per_gpu": T, "global_T": T * world, "C": C, "n": N_STREAMS,
+                      "parallelism": f"token-sharded dp{world}",
+                      "l2": "inputs larger than L2 (x alone 4 GiB), no flush"},
+           "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT, "ms_per_step": round(ms, 4),
+           "steps": steps,
+           "hot_path_hbm_frac": round(bm / (ms * 1e-3) / 1e9 / peaks["hbm_gbs"], 4)}
+    if not args.no_block:
+        out["block"] = run_block(args, torch, dist, world, dev, T=T, C=C,
+                                 workload="MHCLiteBlock fwd+bwd, activation checkpointing, "
+                                          "large token-sharded config (configs[3])")
+        torch.cuda.empty_cache()
+    return out
 
 
 def run_e2e(args, hp, one_step, torch, dist, world, dev):
@@ -642,8 +742,114 @@ def run_e2e(args, hp, one_step, torch, dist, world, dev):
 
 
 # ---------------------------------------------------------------------------
-# CPU restatement (baseline and reference arm)
+# CPU baselines.  The reference's own CPU implementation of the path is its
+# pure-PyTorch block code (src/flash_mhc/block.py:82-148), run from the
+# unmodified reference installed in baseline/_ref; the float32 numpy
+# restatement under oracle/ stands in only when that install is missing.
 # ---------------------------------------------------------------------------
+
+REF_DIR = ROOT / "baseline" / "_ref"
+
+
+def _reference_installed() -> bool:
+    return (REF_DIR / "flash_mhc" / "__init__.py").is_file()
+
+
+def _import_reference():
+    """Import the reference package from baseline/_ref instead of this
+    repository's (both are named ``flash_mhc`` and define the same
+    torch.library namespace, so this process must not have imported ours)."""
+    mod = sys.modules.get("flash_mhc")
+    if mod is not None and REF_DIR.resolve() not in Path(mod.__file__).resolve().parents:
+        raise RuntimeError("this repository's flash_mhc is imported in this process; "
+                           "the reference must run in a process of its own")
+    sys.path[:] = [p for p in sys.path
+                   if Path(p or ".").resolve() not in (ROOT, ROOT / "flash-mhc_b200")]
+    sys.path.insert(0, str(REF_DIR))
+    import flash_mhc as ref  # the reference package
+
+    if REF_DIR.resolve() not in Path(ref.__file__).resolve().parents:
+        raise RuntimeError(f"expected the reference from {REF_DIR}, got {ref.__file__}")
+    return ref
+
+
+def _host_cores() -> int:
+    return len(os.sched_getaffinity(0))
+
+
+def _ref_cpu_hot_path(ref, T, C, steps, warmup, seed=1234):
+    """The hot-path step through the reference's own pure-PyTorch code, float32
+    on the host cores: ``_mhc_pre_map_pytorch`` (K1 as F.rms_norm + F.linear,
+    K2, K3; block.py:82-110) and ``_mhc_post_res_pytorch`` (K4; block.py:112-124)
+    forward, then one autograd backward from upstream gradients of the layer
+    input and the block output (K4, K3, K2 and K1 backward, including the
+    projection-weight gradient).  Inputs have the GPU arm's distributions;
+    ``W_all`` keeps the reference's default init.  Returns per-step seconds."""
+    import torch
+    import torch.nn as nn
+
+    torch.manual_seed(seed)
+    blk = ref.MHCLiteBlock(N_STREAMS, C, nn.Identity())  # the layer itself is not called
+    x = torch.randn(T, N_STREAMS, C).requires_grad_(True)
+    lo = torch.randn(T, C).requires_grad_(True)
+    g_pre = torch.randn(T, C)
+    g_post = torch.randn(T, N_STREAMS, C)
+
+    def step():
+        blk.zero_grad(set_to_none=True)
+        x.grad = None
+        lo.grad = None
+        layer_input, H_merged, h_post = blk._mhc_pre_map_pytorch(x)
+        out = blk._mhc_post_res_pytorch(x, lo, H_merged, h_post)
+        torch.autograd.backward([layer_input, out], [g_pre, g_post])
+
+    for _ in range(warmup):
+        step()
+    times = []
+    for _ in range(steps):
+        t0 = time.perf_counter()
+        step()
+        times.append(time.perf_counter() - t0)
+    return times
+
+
+def _ref_cpu_configs0(ref, iters=5):
+    """the reference's ``MHCLiteBlock`` forward+backward on
+    the CPU (its pure-PyTorch path, block.py:126-148), float32, n=4, C=1024,
+    T=4096, x ~N(0,1), wrapped nn.Linear(1024, 1024, bias=False) ~N(0,0.02),
+    default coefficient-projection init, no activation checkpointing, seed 0.
+    One warm-up iteration, then the median of ``iters``."""
+    import torch
+    import torch.nn as nn
+
+    T, C = 4096, 1024
+    torch.manual_seed(0)
+    layer = nn.Linear(C, C, bias=False)
+    with torch.no_grad():
+        layer.weight.normal_(0.0, 0.02)
+    blk = ref.MHCLiteBlock(N_STREAMS, C, layer).train()
+    x = torch.randn(T, N_STREAMS, C).requires_grad_(True)
+    up = torch.randn(T, N_STREAMS, C)
+
+    def step():
+        blk.zero_grad(set_to_none=True)
+        x.grad = None
+        blk(x).backward(up)  # CPU input: the reference dispatches to _forward_pytorch
+
+    step()
+    ts = []
+    for _ in range(iters):
+        t0 = time.perf_counter()
+        step()
+        ts.append(time.perf_counter() - t0)
+    med = statistics.median(ts)
+    return {"value": round(T / med, 1), "unit": UNIT, "ms_per_iter": round(med * 1e3, 2),
+            "iters": iters, "cores": _host_cores(), "kind": "reference",
+            "workload": "configs[0]: MHCLiteBlock fwd+bwd, pure-PyTorch path, float32, T=4096, "
+                        "C=1024, n=4, Linear(1024, 1024, bias=False) ~N(0,0.02), default init, "
+                        "seed 0",
+            "source": "unmodified reference in baseline/_ref, MHCLiteBlock.forward on CPU "
+                      "(src/flash_mhc/block.py:126-148)"}
 
 def _cpu_worker(args):
     import numpy as np
@@ -667,7 +873,8 @@ def _cpu_worker(args):
 
 
 class CpuPool:
-    """A spawn process pool (one process per core) running the CPU restatement."""
+    """A spawn process pool (one process per core) running the float32 numpy
+    restatement (the fallback when the reference is not installed)."""
 
     def __init__(self, C, workers):
         import multiprocessing as mp
@@ -679,64 +886,112 @@ class CpuPool:
         self.pool.map(_cpu_worker, [(8, C, 0, 1)] * workers)  # imports, first touch
 
     def run(self, tokens_per_worker, reps, seed=100):
-        """(tokens/s, wall s) of every worker running ``reps`` steps of its tokens."""
+        """Wall seconds of every worker running ``reps`` steps of its tokens."""
         t0 = time.perf_counter()
         self.pool.map(_cpu_worker, [(tokens_per_worker, self.C, seed + i, reps)
                                     for i in range(self.workers)])
-        wall = time.perf_counter() - t0
-        return self.workers * tokens_per_worker * reps / wall, wall
+        return time.perf_counter() - t0
 
     def close(self):
         self.pool.close()
         self.pool.join()
 
 
-def cpu_baseline(args):
-    cores = len(os.sched_getaffinity(0))
-    tpw, reps = args.cpu_tokens_per_worker, args.cpu_reps
-    pool = CpuPool(args.C, cores)
-    try:
-        tps, wall = pool.run(tpw, reps)
-    finally:
-        pool.close()
-    return {"value": round(tps, 1), "unit": UNIT, "cores": cores, "kind": "port",
-            "sample": f"{cores} spawn processes x {reps} steps x {tpw} tokens (C={args.C}, n=4) "
-                      f"of the float32 CPU restatement, {wall:.1f} s wall"}
+def workload_config(T, C, world):
+    """The ``config`` object both arms print (the same workload)."""
+    return {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
+            "T_per_gpu": T, "C": C, "n": N_STREAMS, "D": D_OUT,
+            "step": "K1f,K3f,K4f,K4b,K3b,K1b(dx+dW)" + (",allreduce(gW)" if world > 1 else ""),
+            "parallelism": f"token-sharded dp{world}",
+            "l2": f"inputs larger than L2 (x alone {T * N_STREAMS * C * 2 / 2**20:.0f} MiB), "
+                  "no flush"}
 
 
 def run_reference(args):
+    """The reference arm: the reference's own CPU implementation of the path
+    on this box's host cores (rank 0 only; other ranks exit without work).
+
+    With the reference installed in baseline/_ref, each step is
+    ``_ref_cpu_hot_path`` over ``--ref-tokens`` tokens (default: the full
+    per-GPU batch, T) with every host core (torch intra-op threads), plus the
+    configs[0] block timing.  Without it, the float32 numpy restatement on one
+    spawn process per core over a bounded token sample (``kind: "port"``).
+    """
     rank = int(os.environ.get("RANK", "0"))
     world = int(os.environ.get("WORLD_SIZE", "1"))
     if rank != 0:
         return
-    cores = len(os.sched_getaffinity(0))
-    tpw = args.cpu_tokens_per_worker
-    pool = CpuPool(args.C, cores)
-    try:
-        for i in range(args.warmup):
-            pool.run(64, 1, seed=10 + i)
-        times = [pool.run(tpw, 1, seed=1000 + 97 * i)[1] for i in range(args.steps)]
-    finally:
-        pool.close()
-    tok = cores * tpw
-    ms = 1e3 * sum(times) / len(times)
+    cores = _host_cores()
+    T, C = args.T, args.C
+    if _reference_installed() and args.ref_kind == "reference":
+        ref = _import_reference()
+        import torch
+
+        torch.set_num_threads(cores)
+        tok = min(args.ref_tokens or T, T)
+        times = _ref_cpu_hot_path(ref, tok, C, args.steps, args.warmup)
+        ms = 1e3 * sum(times) / len(times)
+        kind = "reference"
+        sample = (f"{tok} of the {T} tokens per step" if tok < T else f"the full {T}-token batch") + (
+            f", float32, torch intra-op threads = {cores}: the reference's pure-PyTorch "
+            "_mhc_pre_map_pytorch + _mhc_post_res_pytorch forward and autograd backward "
+            "(baseline/_ref, src/flash_mhc/block.py:82-124)")
+        source = "unmodified reference installed in baseline/_ref (pure-PyTorch path on CPU)"
+        configs0 = None if args.no_configs0 else _ref_cpu_configs0(ref)
+    else:
+        tpw = args.cpu_tokens_per_worker
+        pool = CpuPool(C, cores)
+        try:
+            for i in range(args.warmup):
+                pool.run(64, 1, seed=10 + i)
+            times = [pool.run(tpw, 1, seed=1000 + 97 * i) for i in range(args.steps)]
+        finally:
+            pool.close()
+        tok = cores * tpw
+        ms = 1e3 * sum(times) / len(times)
+        kind = "port"
+        sample = (f"{tok} of the {T} tokens per step ({cores} spawn processes x {tpw}), "
+                  "float32 numpy restatement of the reference algorithm (oracle/)")
+        source = ("baseline/_ref not installed" if not _reference_installed()
+                  else "numpy restatement requested (--ref-kind port)")
+        configs0 = None
     value = tok / (ms * 1e-3)
     line = {
         "impl": "reference", "metric": METRIC, "value": round(value, 1), "unit": UNIT,
         "n_gpus": world, "steps": args.steps, "warmup": args.warmup,
         "ms_per_step": round(ms, 3), "higher_is_better": True, "scaling": "weak",
-        "vs_baseline": None, "dtype": "f32", "data": "synthetic",
-        "config": {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
-                   "T_per_gpu": args.T, "C": args.C, "n": N_STREAMS, "D": D_OUT,
-                   "sample_tokens_per_step": tok},
-        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": "port",
-                         "sample": f"{tok} of the {args.T} tokens per step ({cores} spawn "
-                                   f"processes x {tpw}), float32 CPU restatement of the "
-                                   "reference algorithm (the reference has no compiled CPU path)"},
+        "vs_baseline": None, "dtype": "f32",
+        "data": "synthetic (seeded N(0,1) x/lo/grads; the reference's default W_all init)",
+        "config": workload_config(T, C, world),
+        "cpu_baseline": {"value": round(value, 1), "unit": UNIT, "cores": cores, "kind": kind,
+                         "sample": sample, "source": source},
         "e2e": {"value": round(value, 1), "unit": UNIT, "h2d_bytes_per_step": 0,
                 "d2h_bytes_per_step": 0},
     }
+    if configs0 is not None:
+        line["cpu_baseline"]["configs0"] = configs0
     print(json.dumps(line), flush=True)
+
+
+def cpu_baseline(args):
+    """``cpu_baseline`` of the GPU arm (rank 0, N = 1): the reference arm run in
+    a child process (this process has imported this repository's flash_mhc,
+    whose torch.library namespace the reference's would clash with) on a
+    bounded token sample, with the GPU hidden from it."""
+    import subprocess
+
+    cmd = [sys.executable, str(Path(__file__).resolve()), "--impl", "reference",
+           "--steps", str(args.cpu_reps), "--warmup", "1", "--T", str(args.T), "--C", str(args.C),
+           "--ref-tokens", str(args.cpu_ref_tokens),
+           "--cpu-tokens-per-worker", str(args.cpu_tokens_per_worker)]
+    env = dict(os.environ, CUDA_VISIBLE_DEVICES="", RANK="0", WORLD_SIZE="1")
+    r = subprocess.run(cmd, capture_output=True, text=True, env=env, timeout=900, cwd=ROOT)
+    if r.returncode != 0:
+        return {"value": None, "unit": UNIT, "cores": _host_cores(), "kind": "reference",
+                "sample": None, "error": (r.stderr or r.stdout)[-500:]}
+    cb = json.loads(r.stdout.strip().splitlines()[-1])["cpu_baseline"]
+    cb["steps"] = args.cpu_reps
+    return cb
 
 
 def run_reference_triton(args):
@@ -810,16 +1065,17 @@ def run_reference_triton(args):
     torch.cuda.synchronize()
     tune_s = time.time() - t_tune
     s, e = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(args.steps):
-        step()
-    e.record()
-    torch.cuda.synchronize()
-    ms = s.elapsed_time(e) / args.steps
-    ev = {}
-    for _ in range(5):
-        step(ev)
-    torch.cuda.synchronize()
+    with ClockSampler(_physical_gpu_indices(1)) as clk:
+        s.record()
+        for _ in range(args.steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
+        ms = s.elapsed_time(e) / args.steps
+        ev = {}
+        for _ in range(5):
+            step(ev)
+        torch.cuda.synchronize()
     kernels = {k: round(sum(a.elapsed_time(b) for a, b in v) / len(v), 4) for k, v in ev.items()}
     line.update({
         "value": round(T / (ms * 1e-3), 1), "n_gpus": 1, "steps": args.steps,
@@ -828,6 +1084,7 @@ def run_reference_triton(args):
         "config": {"workload": "kernel-level hot path fwd+bwd (configs[1] shapes)",
                    "T_per_gpu": T, "C": C, "n": n, "D": D},
         "kernels_ms": kernels,
+        "clocks": clk.summary(),
         "autotune": os.environ.get("FLASH_MHC_TRITON_AUTOTUNE", "default"),
         "warmup_s_incl_autotune": round(tune_s, 1),
         "source": "unmodified reference installed in baseline/_ref, torch.ops.flash_mhc (Triton)",
@@ -851,16 +1108,17 @@ def run_reference_triton(args):
         for _ in range(3):
             bstep()
         torch.cuda.synchronize()
-        s.record()
-        for _ in range(10):
-            bstep()
-        e.record()
-        torch.cuda.synchronize()
+        with ClockSampler(_physical_gpu_indices(1)) as bclk:
+            s.record()
+            for _ in range(10):
+                bstep()
+            e.record()
+            torch.cuda.synchronize()
         bms = s.elapsed_time(e) / 10
         line["block"] = {"config": {"workload": "MHCLiteBlock fwd+bwd, activation checkpointing "
                                                 "(configs[2])", "T_per_gpu": Tb, "C": Cb, "n": n},
                          "value": round(Tb / (bms * 1e-3), 1), "unit": UNIT,
-                         "ms_per_step": round(bms, 4), "steps": 10}
+                         "ms_per_step": round(bms, 4), "steps": 10, "clocks": bclk.summary()}
     print(json.dumps(line), flush=True)
 
 
@@ -874,8 +1132,17 @@ def main():
                          "own Triton kernels on this GPU from baseline/_ref (comparison line)")
     ap.add_argument("--T", type=int, default=65536, help="tokens per GPU")
     ap.add_argument("--C", type=int, default=1024)
-    ap.add_argument("--cpu-tokens-per-worker", type=int, default=1024)
-    ap.add_argument("--cpu-reps", type=int, default=4)
+    ap.add_argument("--cpu-tokens-per-worker", type=int, default=1024,
+                    help="tokens per spawn process of the numpy fallback")
+    ap.add_argument("--cpu-reps", type=int, default=3, help="timed steps of cpu_baseline")
+    ap.add_argument("--cpu-ref-tokens", type=int, default=16384,
+                    help="tokens per step of the reference code in cpu_baseline")
+    ap.add_argument("--ref-tokens", type=int, default=0,
+                    help="tokens per step of the reference arm (0: the full per-GPU batch)")
+    ap.add_argument("--ref-kind", choices=["reference", "port"], default="reference",
+                    help="reference arm: the reference's own code (baseline/_ref) or the numpy port")
+    ap.add_argument("--no-configs0", action="store_true",
+                    help="reference arm: skip the configs[0] block timing")
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-block", action="store_true", help="skip the MHCLiteBlock measurement")
     ap.add_argument("--block-T", type=int, default=65536, help="tokens per GPU for the block")
@@ -885,6 +1152,14 @@ def main():
     ap.add_argument("--no-e2e", action="store_true",
                     help="skip the host-buffer e2e leg (its pinned buffers grow with --T/--C)")
     ap.add_argument("--small-T", type=int, default=8192)
+    ap.add_argument("--no-large", action="store_true",
+                    help="skip the large token-sharded config (configs[3])")
+    ap.add_argument("--large-T", type=int, default=131072, help="tokens per GPU, configs[3]")
+    ap.add_argument("--large-C", type=int, default=4096)
+    ap.add_argument("--nccl-max-ctas", type=int, default=0,
+                    help="NCCL communicator max_ctas (0: NCCL's default)")
+    ap.add_argument("--nccl-nvls-ctas", type=int, default=0,
+                    help="NCCL communicator nvls_ctas (0: NCCL's default)")
     args = ap.parse_args()
     if args.warmup < 3 and args.impl == "ours":
         print("note: the timing rules ask for >= 3 warm-up steps", file=sys.stderr)

@@ -216,6 +216,22 @@ int fmhc_k1_fwd(const void *x, const void *W, void *out, float *inv_rms, int64_t
   return check_launch(w);
 }
 
+int fmhc_debug_k1_fwd_lost_copy(const void *x, const void *W, void *out, float *inv_rms,
+                                int64_t T, int64_t nC, void *stream) {
+  const char *w = "fmhc_debug_k1_fwd_lost_copy";
+  if (int e = check_k1(w, T, nC, 32)) return e;
+  if (T == 0) return fail(FMHC_ERR_INVALID_ARGUMENT, "%s: needs T >= 1", w);
+  FMHC_REQUIRE_PTR(w, x); FMHC_REQUIRE_PTR(w, W); FMHC_REQUIRE_PTR(w, out);
+  FMHC_REQUIRE_PTR(w, inv_rms);
+  if (!fmhc::k1_tc_fwd_supported(x, W, out, inv_rms, T, nC, 32))
+    return fail(FMHC_ERR_INVALID_ARGUMENT,
+                "%s: needs the tensor-core K1 forward (nC %% 64 == 0, 16-byte aligned x, W, out, "
+                "a B200)", w);
+  if (int e = fmhc::launch_k1_tc_fwd_lost_copy(x, W, out, inv_rms, T, int(nC), (cudaStream_t)stream))
+    return fail(e, "%s: %s", w, fmhc::k1_tc_error());
+  return check_launch(w);
+}
+
 int fmhc_k1_bwd_dx(const void *grad_out, const void *x, const void *W, const void *proj,
                    const float *inv_rms, void *grad_x, int64_t T, int64_t nC, int64_t D,
                    void *stream) {

@@ -38,6 +38,12 @@ int launch_k1_tc_bwd(const void *go, const void *x, const void *W, const void *p
                      const float *inv_rms, void *gx, void *gW, void *ws, int64_t ws_bytes,
                      int64_t T, int nC, cudaStream_t s);
 
+// Test hook: the persistent tensor-core forward in which CTA 0 loses its first
+// copy, so its waits on that stage expire (see k1_fwd_tc_kernel's LOSE_COPY).
+// Same preconditions as launch_k1_tc_fwd; the output is not meaningful.
+int launch_k1_tc_fwd_lost_copy(const void *x, const void *W, void *out, float *inv_rms,
+                               int64_t T, int nC, cudaStream_t s);
+
 // Reads and clears the per-device error word set by expired bounded waits.
 int read_device_error(unsigned *code);
 

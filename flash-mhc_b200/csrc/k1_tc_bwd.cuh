@@ -490,6 +490,13 @@ k1_bwd_dw_reduce_kernel(const float *__restrict__ part, __nv_bfloat16 *__restric
     for (int u = 0; u < 8; ++u)
       if (i + u < n) acc += v[u];
   }
+  // A CTA of the main kernel whose bounded wait gave up has not written its
+  // partials, so the sum would mix in whatever the workspace held before.
+  // While the device error word is set (until fmhc_check_device_error reads
+  // and clears it) grad_W is therefore written as NaN, never as a plausible
+  // value.  The main kernel completed before this grid passed pdl_wait(), so
+  // its error store is visible here.
+  if (*reinterpret_cast<volatile unsigned *>(&sm100::g_device_error) != 0u) acc = __int_as_float(0x7fc00000);
   gW[int64_t(d) * nC + int64_t(kc) * kBwdBK + kl] = __float2bfloat16_rn(acc);
 }
 

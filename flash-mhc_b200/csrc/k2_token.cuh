@@ -12,12 +12,15 @@
 //                                                        flattened permutation matrices)
 //   H_merged= H_res - h_post (outer) h_pre
 // (reference: src/flash_mhc/block.py:150-170).  The reference evaluates this
-// in the input dtype (bf16): alphas and bias are cast to bf16 and h_pre,
-// h_post, H_merged are stored as bf16 before the f32 copies that K3/K4
-// consume.  Here the parameters are rounded to bf16 the same way and the
-// three outputs are rounded to bf16 (then stored as f32), while the
-// intermediate arithmetic runs in f32 (the reference rounds every
-// intermediate op to bf16; the results agree to bf16 rounding).
+// in the input dtype (bf16): alphas and bias are cast to bf16, every
+// intermediate op rounds to bf16, and h_pre, h_post, H_merged are stored as
+// bf16 before the f32 copies that K3/K4 consume.  Here the parameters are
+// rounded to bf16 the same way (the reference's `.to(dt)`), the logits are
+// the bf16 values K1 stores, and everything after that runs and is stored in
+// f32: the coefficients are those of the reference's float32 path on the same
+// logits, to f32 rounding.  (Rounding them to bf16 as the bf16 eager code does
+// costs up to 2^-9 of each coefficient, which the post-mix multiplies by
+// |x| + |layer_output|; in f32 they stay within 1e-4 of the float32 block.)
 #pragma once
 
 #include "fmhc_common.cuh"
@@ -61,7 +64,7 @@ __device__ __forceinline__ void stage_params(ParamSmem &sm, const K2Params &P, i
 // Forward intermediates of one token.
 struct Tok {
   float spre[4], spost[4];  // sigmoids (unrounded)
-  float hpre[4], hpost[4];  // bf16-rounded outputs
+  float hpre[4], hpost[4];  // outputs
   float a[kNF];             // softmax
 };
 
@@ -71,9 +74,9 @@ __device__ __forceinline__ void forward_token(const ParamSmem &sm, const float (
 #pragma unroll
   for (int i = 0; i < 4; ++i) {
     k.spre[i] = sigm(ap * v[i] + b[i]);
-    k.hpre[i] = bf16r(k.spre[i]);
+    k.hpre[i] = k.spre[i];
     k.spost[i] = sigm(aq * v[4 + i] + b[4 + i]);
-    k.hpost[i] = bf16r(2.f * k.spost[i]);
+    k.hpost[i] = 2.f * k.spost[i];
   }
   float m = -INFINITY;
 #pragma unroll
@@ -92,8 +95,7 @@ __device__ __forceinline__ void forward_token(const ParamSmem &sm, const float (
   for (int j = 0; j < kNF; ++j) k.a[j] *= inv;
 }
 
-// h_pre, h_post (T, 4) and H_merged (T, 4, 4) of token t, f32 holding bf16
-// values.  Returns the h_pre written.
+// h_pre, h_post (T, 4) and H_merged (T, 4, 4) of token t, in f32.  Returns the h_pre written.
 __device__ __forceinline__ float4 store_coeffs(const ParamSmem &sm, const float (&v)[32],
                                              float4 *__restrict__ h_pre,
                                              float4 *__restrict__ h_post,
@@ -103,10 +105,10 @@ __device__ __forceinline__ float4 store_coeffs(const ParamSmem &sm, const float 
   float Hm[16];
 #pragma unroll
   for (int e = 0; e < 16; ++e) {
-    float acc = 0.f;  // bf16 softmax output times the bf16 permutation rows, f32 accumulate
+    float acc = 0.f;  // softmax output times the permutation rows, f32 accumulate
 #pragma unroll
-    for (int j = 0; j < kNF; ++j) acc = fmaf(bf16r(k.a[j]), sm.perm[j * 16 + e], acc);
-    Hm[e] = bf16r(bf16r(acc) - bf16r(k.hpost[e >> 2] * k.hpre[e & 3]));
+    for (int j = 0; j < kNF; ++j) acc = fmaf(k.a[j], sm.perm[j * 16 + e], acc);
+    Hm[e] = fmaf(-k.hpost[e >> 2], k.hpre[e & 3], acc);
   }
   const float4 hp = make_float4(k.hpre[0], k.hpre[1], k.hpre[2], k.hpre[3]);
   h_pre[t] = hp;

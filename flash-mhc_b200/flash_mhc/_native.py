@@ -28,6 +28,7 @@ _SIGNATURES = {
     "fmhc_version": [],
     "fmhc_check_device_error": [ctypes.POINTER(ctypes.c_int)],
     "fmhc_k1_fwd": [_vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
+    "fmhc_debug_k1_fwd_lost_copy": [_vp, _vp, _vp, _vp, _i64, _i64, _vp],
     "fmhc_k1_bwd_dx": [_vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _vp],
     "fmhc_k1_bwd_workspace_size": [_i64, _i64, _i64],
     "fmhc_k1_bwd": [_vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _i64, _i64, _i64, _i64, _vp],

@@ -229,7 +229,8 @@ class MHCLiteBlock(nn.Module):
 
     # ------------------------------------------------------------- fused
     def _mhc_coeffs_triton(self, x_streams: torch.Tensor):
-        """K1 + K2 through the ops (f32 coefficients, rounded to bf16 like the reference)."""
+        """K1 + K2 through the ops: f32 coefficients from the bf16 logits, with the
+        parameters rounded to bf16 as the reference's ``.to(dt)`` does."""
         dt = x_streams.dtype
         T = x_streams.shape[0]
         x_flat = x_streams.reshape(T, self.nC)

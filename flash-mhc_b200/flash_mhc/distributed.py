@@ -90,3 +90,127 @@ def allreduce_gradients(module: torch.nn.Module, group=None, average: bool = Tru
         return work, finish
     finish()
     return None
+
+
+class BucketedGradReducer:
+    """Data-parallel gradient all-reduce that overlaps the backward pass.
+
+    The parameters of ``module`` are split into buckets (``buckets``: lists of
+    parameters, in the order the backward produces them; by default, for an
+    ``MHCLiteBlock``, the wrapped layer's parameters first and the block's own
+    ``W_all`` / alphas second).  A post-accumulate-grad hook counts each
+    bucket's gradients as the backward writes them; once a bucket is complete
+    its gradients are packed into a preallocated buffer of ``reduce_dtype``
+    (float32 by default) with one multi-tensor copy, and an asynchronous
+    all-reduce of that buffer starts.  In the fused block the layer's gradient
+    is ready before the K3/K2/K1 backward and the grad_x combination run, so
+    its (large) reduction proceeds on NCCL's stream while those kernels
+    compute; the block's own gradients (small) are returned with grad_x at the
+    end of the backward.  Buckets are launched strictly in bucket order (a bucket
+    that completes early waits for the ones before it), so every rank issues
+    the same collectives in the same order.
+
+    Call ``finish()`` after ``backward()``: it launches any bucket still
+    pending (parameters without a gradient count as zero), makes the current
+    stream wait for the reductions, scales by 1/world_size (``average``) and
+    writes the sums back into ``.grad`` with one multi-tensor copy per bucket.
+    """
+
+    def __init__(self, module: torch.nn.Module, buckets=None, group=None, average: bool = True,
+                 reduce_dtype: torch.dtype = torch.float32):
+        self.group = group
+        self.average = average
+        self.reduce_dtype = reduce_dtype
+        if buckets is None:
+            buckets = default_buckets(module)
+        self.buckets = []
+        seen = set()
+        for plist in buckets:
+            plist = [p for p in plist if p.requires_grad and id(p) not in seen]
+            seen.update(id(p) for p in plist)
+            if plist:
+                self.buckets.append({"params": plist, "ready": 0, "work": None, "buf": None,
+                                     "views": None})
+        rest = [p for p in module.parameters() if p.requires_grad and id(p) not in seen]
+        if rest:
+            self.buckets.append({"params": rest, "ready": 0, "work": None, "buf": None,
+                                 "views": None})
+        self._index = {}
+        self._handles = []
+        for bi, b in enumerate(self.buckets):
+            for p in b["params"]:
+                self._index[id(p)] = bi
+                self._handles.append(p.register_post_accumulate_grad_hook(self._hook))
+        self._next = 0  # first bucket not launched yet
+
+    def _buffer(self, b, device):
+        if b["buf"] is None:
+            total = sum(p.numel() for p in b["params"])
+            buf = torch.empty(total, dtype=self.reduce_dtype, device=device)
+            views, off = [], 0
+            for p in b["params"]:
+                views.append(buf[off:off + p.numel()].view(p.shape))
+                off += p.numel()
+            b["buf"], b["views"] = buf, views
+        return b["buf"]
+
+    def _launch(self, b):
+        params = b["params"]
+        dev = next((p.grad.device for p in params if p.grad is not None), params[0].device)
+        buf = self._buffer(b, dev)
+        have = [(v, p.grad) for v, p in zip(b["views"], params) if p.grad is not None]
+        if len(have) < len(params):
+            buf.zero_()
+        if have:
+            torch._foreach_copy_([v for v, _ in have], [g for _, g in have])
+        b["work"] = dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+
+    def _launch_ready(self):
+        while self._next < len(self.buckets):
+            b = self.buckets[self._next]
+            if b["ready"] < len(b["params"]):
+                return
+            self._launch(b)
+            self._next += 1
+
+    def _hook(self, p):
+        self.buckets[self._index[id(p)]]["ready"] += 1
+        self._launch_ready()
+
+    def finish(self) -> None:
+        for b in self.buckets[self._next:]:
+            b["ready"] = len(b["params"])
+        self._launch_ready()
+        world = dist.get_world_size(self.group)
+        for b in self.buckets:
+            b["work"].wait()
+            if self.average and world > 1:
+                b["buf"].mul_(1.0 / world)
+            grads = []
+            for p, v in zip(b["params"], b["views"]):
+                if p.grad is None:
+                    p.grad = torch.empty_like(p)
+                grads.append(p.grad)
+            torch._foreach_copy_(grads, b["views"])
+            b["ready"], b["work"] = 0, None
+        self._next = 0
+
+    def remove(self) -> None:
+        """Unregister the hooks."""
+        for h in self._handles:
+            h.remove()
+        self._handles = []
+
+
+def default_buckets(module: torch.nn.Module) -> list:
+    """Buckets in backward order for an ``MHCLiteBlock``: the wrapped layer's
+    parameters (their gradients are ready after the layer's backward), then the
+    block's own parameters (ready after the K2 and K1 backward).  Any other
+    module: one bucket of all its parameters."""
+    layer = getattr(module, "layer", None)
+    if isinstance(layer, torch.nn.Module):
+        lp = [p for p in layer.parameters() if p.requires_grad]
+        lids = {id(p) for p in lp}
+        own = [p for p in module.parameters() if p.requires_grad and id(p) not in lids]
+        return [lp, own]
+    return [[p for p in module.parameters() if p.requires_grad]]

@@ -61,6 +61,19 @@ FMHC_API const char *fmhc_version(void);
  * reference's Triton kernels have no device-side failure reporting. */
 FMHC_API int fmhc_check_device_error(int *code);
 
+/* Test hook for the failure path above (not for production use): the
+ * tensor-core K1 forward (x (T, nC) bf16, W (32, nC) bf16, 16-byte aligned,
+ * nC % 64 == 0, T >= 1) in which the first CTA arms its first pipeline stage
+ * for a copy that it never issues.  Its waits on that stage expire after the
+ * bound (about 1 s each, two in a row), it records a site code in the error
+ * word, frees its tensor memory and returns; the other CTAs finish normally.
+ * The outputs are not meaningful; the context stays usable, so a following
+ * fmhc_check_device_error reports the code and later calls run normally.
+ * While the word is set, fmhc_k1_bwd and fmhc_k1_bwd_noalloc write grad_W as
+ * NaN.  No reference counterpart. */
+FMHC_API int fmhc_debug_k1_fwd_lost_copy(const void *x, const void *W, void *out,
+                                         float *inv_rms, int64_t T, int64_t nC, void *stream);
+
 /* ------------------------------------------------------------------------
  * K1 forward: fused RMSNorm + thin projection.
  *   inv_rms[t] = rsqrt(sum_k x[t,k]^2 / nC + 1e-6)                    (f32)
@@ -96,7 +109,9 @@ FMHC_API int fmhc_k1_bwd_dx(const void *grad_out, const void *x, const void *W,
  * fmhc_k1_bwd_workspace_size(T, nC, D) bytes (256-byte aligned; the size
  * depends on the current device's SM count); its contents on entry do not
  * matter and the result does not depend on them (the grad_W reduction order
- * is fixed, so results are bitwise reproducible).
+ * is fixed, so results are bitwise reproducible).  While the device error
+ * word is set (a bounded wait expired; see fmhc_check_device_error), grad_W
+ * is written as NaN instead of a sum of partials that were not all written.
  * Replaces the K1 autograd formula (src/flash_mhc/ops.py:678-685): the
  * bwd-dx op plus the separate cuBLAS matmul for grad_W (ops.py:683-684).
  */
@@ -121,10 +136,13 @@ FMHC_API int fmhc_k1_bwd(const void *grad_out, const void *x, const void *W,
  * partials alone, at most 18.5 MiB at any T; the CUDA-core path needs up to
  * 2 KiB x nC, so it fits up to nC = 16384.  Larger calls fail with
  * FMHC_ERR_WORKSPACE and should use fmhc_k1_bwd.  Every GPU that loads the
- * library holds the 32 MiB until the process exits.  The first call on each
- * device looks up the array's device address; make it before any stream
- * capture.  All calls share the array, so calls that overlap on the same GPU
- * race and must not be issued; the array's previous contents never matter.
+ * library holds the 32 MiB until the process exits.  The first call in each
+ * CUDA context (once per device, and again after a device reset creates a new
+ * context) looks up the array's device address; make the first call on each
+ * device before any stream capture.  All calls share the array, so calls that
+ * overlap on the same GPU race and must not be issued; when a call succeeds
+ * the array's previous contents do not matter (after an expired wait grad_W
+ * is NaN, as for fmhc_k1_bwd).
  * No counterpart in the reference (its ops always allocate through torch).
  */
 FMHC_API int fmhc_k1_bwd_noalloc(const void *grad_out, const void *x, const void *W,

@@ -17,6 +17,10 @@ seeds.  Outputs (all small):
 * ``block_fp32.npz`` / ``block_bf16.npz`` / ``block_outlier_fp32.npz``:
   ``MHCLiteBlock._forward_pytorch`` (src/flash_mhc/block.py:126-148) forward,
   grad_x and every parameter gradient, plus the K2 intermediates.
+* ``block_cfg0_fp32.npz`` / ``block_grid_fp32.npz``: the same float32 block
+  on bf16-valued seeded inputs and parameters (``block_inputs.py``), at
+  BASELINE configs[0] (T=4096, C=1024, default init, Linear(1024, 1024)) and
+  at a small stress case; per-token outputs for a stored subset of rows.
 * ``reference_api.json``: op schemas, fake-impl output dtypes, the block's
   state_dict names/shapes and ``build_permutation_matrices(4)``.
 
@@ -124,6 +128,55 @@ def _block_case(ref_pkg, tc, dtype, seed, *, T=48, C=32, outlier=False, ckpt=Fal
     return res
 
 
+def _grid_case(ref_pkg, name):
+    """The reference's float32 ``_forward_pytorch`` on bf16-valued inputs and
+    parameters (``block_inputs.CASES[name]``), so a bf16 path can be fed the
+    very same values.  Per-token tensors are stored for ``stored_rows`` only
+    (the block is token-local); parameter gradients in full, the wrapped
+    layer's for 8 rows."""
+    from block_inputs import CASES, block_case_inputs, stored_rows
+
+    T, C, seed, wl_std, alphas, gelu, n_rows = CASES[name]
+    inp = block_case_inputs(T, C, seed, wl_std, alphas)
+
+    class _Layer(torch.nn.Module):
+        def __init__(self):
+            super().__init__()
+            self.proj = torch.nn.Linear(C, C, bias=False)
+
+        def forward(self, x):
+            y = self.proj(x)
+            return torch.nn.functional.gelu(y) if gelu else y
+
+    layer = _Layer()
+    blk = ref_pkg.MHCLiteBlock(4, C, layer)
+    with torch.no_grad():
+        for p, v in zip((blk.alpha_pre, blk.alpha_post, blk.alpha_res), inp["alphas"]):
+            p.fill_(float(v))
+        blk.W_all.weight.copy_(torch.from_numpy(inp["W"]))
+        blk.W_all.bias.copy_(torch.from_numpy(inp["bias"]))
+        layer.proj.weight.copy_(torch.from_numpy(inp["Wl"]))
+    blk = blk.float().train()
+    x = torch.from_numpy(inp["x"]).float().requires_grad_(True)
+    out = blk._forward_pytorch(x)
+    (out * torch.from_numpy(inp["g"]).float()).sum().backward()
+    with torch.no_grad():
+        h_pre, h_post, H = blk._mhc_coeffs_pytorch(x.detach())
+        li = blk._mhc_pre_map_pytorch(x.detach())[0]
+    rows = stored_rows(T, n_rows)
+    wl_rows = np.arange(0, C, max(1, C // 8))[:8]
+    r = lambda t: _np(t)[rows]  # noqa: E731
+    return {
+        "T": T, "C": C, "seed": seed, "wl_std": wl_std, "alphas": np.asarray(alphas),
+        "gelu": int(gelu), "rows": rows, "wl_rows": wl_rows,
+        "out": r(out), "grad_x": r(x.grad), "h_pre": r(h_pre), "h_post": r(h_post),
+        "H_merged": r(H), "layer_input": r(li),
+        "g_W": _np(blk.W_all.weight.grad), "g_bias": _np(blk.W_all.bias.grad),
+        "g_alpha_pre": _np(blk.alpha_pre.grad), "g_alpha_post": _np(blk.alpha_post.grad),
+        "g_alpha_res": _np(blk.alpha_res.grad), "g_Wl_rows": _np(layer.proj.weight.grad)[wl_rows],
+    }
+
+
 def _api(ref_pkg):
     lib_ops = [
         "fused_rmsnorm_project", "fused_rmsnorm_project_bwd_dx", "fused_pre_map",
@@ -168,15 +221,26 @@ def _api(ref_pkg):
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--reference-root", required=True)
+    ap.add_argument("--only-grid", action="store_true",
+                    help="write only the bf16-grid block fixtures (block_inputs.CASES)")
     args = ap.parse_args()
     root = Path(args.reference_root)
     sys.path.insert(0, str(root / "src"))
     sys.path.insert(0, str(root / "tests"))
+    sys.path.insert(0, str(HERE))
+    sys.path.insert(0, str(HERE.parents[1]))  # the repository root, for oracle/
     import flash_mhc as ref_pkg  # the reference package
     import test_correctness as tc
 
     assert "flash-mhc_b200" not in ref_pkg.__file__
     torch.set_num_threads(4)
+    from block_inputs import CASES
+
+    for name in CASES:
+        np.savez_compressed(HERE / f"{name}.npz", **_grid_case(ref_pkg, name))
+    if args.only_grid:
+        print("wrote the bf16-grid block fixtures to", HERE)
+        return
     np.savez_compressed(HERE / "ops_fp32.npz", **_ops_case(tc, torch.float32, 1))
     np.savez_compressed(HERE / "ops_bf16.npz", **_ops_case(tc, torch.bfloat16, 2))
     np.savez_compressed(HERE / "block_fp32.npz", **_block_case(ref_pkg, tc, torch.float32, 3))

@@ -4,7 +4,8 @@
 * every rank runs MHCLiteBlock on its token shard (pure-PyTorch path on CPU,
   the same math the fused CUDA path restates) and allreduce_gradients sums the
   parameter gradients in one bucket: the result equals the single-process
-  full-batch gradient (the path's only exchange);
+  full-batch gradient (the path's only exchange); BucketedGradReducer does the
+  same per bucket from post-accumulate-grad hooks during the backward;
 * failure detection on the host: a rank that dies before the collective makes
   the surviving rank's all-reduce fail after the process-group timeout instead
   of hanging.
@@ -25,7 +26,8 @@ import torch.multiprocessing as mp
 import torch.nn as nn
 
 from flash_mhc import MHCLiteBlock
-from flash_mhc.distributed import allreduce_gradients, shard_bounds, shard_tokens
+from flash_mhc.distributed import (BucketedGradReducer, allreduce_gradients, shard_bounds,
+                                   shard_tokens)
 
 
 def _free_port() -> int:
@@ -85,6 +87,21 @@ def _worker(rank, world, port, out_dir, mode):
         blk = _model(0)
         x, g = _data()
         xs, gs = shard_tokens(x, rank, world), shard_tokens(g, rank, world)
+        if mode == "bucketed":
+            # two steps through the overlapped reducer: the hooks launch each
+            # bucket during backward; the second step checks the state resets
+            red = BucketedGradReducer(blk)
+            assert len(red.buckets) == 2  # the wrapped layer, then the block's own
+            for _ in range(2):
+                blk.zero_grad(set_to_none=True)
+                (blk(xs) * gs).sum().backward()
+                red.finish()
+            red.remove()
+            grads = {n: p.grad.clone() for n, p in blk.named_parameters()}
+            torch.save({"grads": grads}, os.path.join(out_dir, f"r{rank}.pt"))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         out = blk(xs)
         (out * gs).sum().backward()
         if mode == "async":
@@ -127,12 +144,12 @@ def _reference_grads():
     return {n: p.grad.clone() for n, p in blk.named_parameters()}
 
 
-@pytest.mark.parametrize("mode", ["sum", "async", "avg"])
+@pytest.mark.parametrize("mode", ["sum", "async", "avg", "bucketed"])
 def test_token_sharded_grads_equal_full_batch(mode):
     out_dir, procs = _run(mode)
     assert all(p.exitcode == 0 for p in procs)
     ref = _reference_grads()
-    scale = 0.5 if mode == "avg" else 1.0
+    scale = 0.5 if mode in ("avg", "bucketed") else 1.0
     for r in range(2):
         got = torch.load(os.path.join(out_dir, f"r{r}.pt"))["grads"]
         for n, t in ref.items():

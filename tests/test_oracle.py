@@ -124,6 +124,34 @@ def test_block_fp32_matches_reference(name):
         assert_close(gk, np.reshape(gr[k], ref.shape), ref, 1e-4 * scale, 1e-4)
 
 
+@pytest.mark.parametrize("name", ["block_grid_fp32", "block_cfg0_fp32"])
+def test_block_grid_fixtures_match_oracle(name):
+    """The bf16-grid fixtures (the reference's float32 block on bf16-valued
+    seeded inputs, tests/golden/block_inputs.py) against the float64 block
+    restatement: forward, coefficients and every gradient to f32 accuracy."""
+    from tests.golden.block_inputs import block_case_inputs
+
+    g = load_golden(name)
+    T, C, seed = int(g["T"]), int(g["C"]), int(g["seed"])
+    inp = block_case_inputs(T, C, seed, float(g["wl_std"]), tuple(g["alphas"]))
+    params = dict(alpha_pre=inp["alphas"][0], alpha_post=inp["alphas"][1],
+                  alpha_res=inp["alphas"][2], W=inp["W"], bias=inp["bias"],
+                  perm=O.build_permutation_matrices(4)[0], Wl=inp["Wl"])
+    layer = "linear_gelu" if int(g["gelu"]) else "linear"
+    r = O.block_forward_backward(params, inp["x"], inp["g"], rms_eps=float(np.finfo(np.float32).eps),
+                                 layer=layer)
+    rows = g["rows"]
+    for k in ("out", "grad_x", "h_pre", "h_post", "H_merged", "layer_input"):
+        assert_close(k, r[k][rows], g[k], 1e-5, 1e-4)
+    gr = r["grads"]
+    for k, gk in (("alpha_pre", "g_alpha_pre"), ("alpha_post", "g_alpha_post"),
+                  ("alpha_res", "g_alpha_res"), ("W", "g_W"), ("bias", "g_bias")):
+        ref = g[gk]
+        assert_close(gk, np.reshape(gr[k], ref.shape), ref, 1e-4 * max(1.0, float(np.abs(ref).max())), 1e-4)
+    ref = g["g_Wl_rows"]
+    assert_close("g_Wl", gr["Wl"][g["wl_rows"]], ref, 1e-4 * max(1.0, float(np.abs(ref).max())), 1e-4)
+
+
 def test_block_bf16_matches_reference_within_bf16_tolerance():
     """The reference's bf16 path rounds every intermediate; the oracle computes
     in float64 from the same bf16 inputs.  The reference's own end-to-end

@@ -12,6 +12,9 @@ This test calls both entry points through the C ABI (ctypes) on the same
 inputs and checks that the allocation-free one matches the workspace one within
 the tolerances the other GPU tests use (bf16: 2e-2 + 1e-2*|ref|), on two calls
 in a row (the second reuses whatever the first left in the shared scratch).
+Before the checked calls of every case, one call on unrelated inputs of the
+largest shape fills the scratch with other values, so a read of a scratch
+value the checked call did not write would show, whichever case runs alone.
 It is collected last on purpose (file name), so a failure here never hides
 another test's result.
 """
@@ -75,6 +78,15 @@ def _no_alloc(L, go, x, W, proj, inv):
     return gx, gW
 
 
+def _fill_scratch(L):
+    """One call on unrelated inputs of the largest shape (its grad_W partials
+    cover the most scratch), leaving their values in the shared array."""
+    go, x, W, proj, inv = _inputs(65536, 4096, seed=999)
+    go.mul_(3.0)
+    _no_alloc(L, go, x, W, proj, inv)
+    torch.cuda.synchronize()
+
+
 @pytest.mark.parametrize("T,nC", [(65536, 4096), (4097, 1024), (300, 400)])
 def test_no_alloc_matches_workspace_entry_point(T, nC):
     import flash_mhc  # noqa: F401  (registers the ops used to make inputs)
@@ -82,6 +94,7 @@ def test_no_alloc_matches_workspace_entry_point(T, nC):
     L = _lib()
     go, x, W, proj, inv = _inputs(T, nC, seed=T + nC)
     ref_gx, ref_gW = _with_workspace(L, go, x, W, proj, inv)
+    _fill_scratch(L)
     for _ in range(2):  # two calls in a row share the scratch array
         gx, gW = _no_alloc(L, go, x, W, proj, inv)
         torch.cuda.synchronize()
