@@ -21,15 +21,8 @@
 //              (async-proxy) write, so each thread issues fence.proxy.async
 //              before its release arrive; without it, loads still pending at
 //              the arrive were seen returning the next fill's data.
-// Tiles are dealt in rounds (fwd_tile below): each CTA gets q or q + 1 of the
-// U 32-row units (balanced to within one unit) and takes up to 4 of them per
-// round as one contiguous tile of <= 128 rows, the CTAs' tiles of a round
-// lying side by side in one window of the tokens.  So the whole grid sweeps
-// the tokens together, round by round, in the direction REV picks (the
-// launch uses the backward sweep: the previous kernel of the fwd+bwd step,
-// K1's backward, sweeps forward and leaves the last tokens in L2, and the
-// next one, K3's forward, starts at token 0).  Partial tiles load only the
-// 32-row boxes they need.  Which CTA handles a token changes no result bit.
+// Each CTA owns a contiguous token range in 32-row units (balanced to within
+// 32 rows across CTAs); partial tiles load only the 32-row boxes they need.
 // Every mbarrier wait is bounded (sm100_ptx.cuh): on expiry the kernel records
 // an error code, drains its copies and MMAs (bounded), frees TMEM and returns.
 #include <cuda.h>
@@ -97,31 +90,6 @@ struct alignas(1024) FwdSmem {
 enum : unsigned { kSiteProdEmpty = 0x101, kSiteMmaFull = 0x102, kSiteMmaTempty = 0x103,
                   kSiteEpiFull = 0x104, kSiteEpiTfull = 0x105, kSiteDrain = 0x106 };
 
-// Round r's tile of CTA c (of G) over U 32-row units: false once the CTA has
-// none left.  CTA c owns n_c = q + (c < rem) units (q = U / G, rem = U % G) and
-// takes min(4, n_c - 4r) of them in round r; after r rounds a CTA with n units
-// has consumed min(4r, n), so round r's window starts at
-// base = rem min(4r, q + 1) + (G - rem) min(4r, q), and within it CTA c's tile
-// follows the tiles of CTAs 0 .. c-1.  REV mirrors the unit index, so the
-// sweep runs from the last token to the first.
-template <bool REV>
-__device__ __forceinline__ bool fwd_tile(int64_t U, int64_t T, int r, int64_t &row0,
-                                         int64_t &rows) {
-  const int64_t G = gridDim.x, c = blockIdx.x;
-  const int64_t q = U / G, rem = U % G;
-  const int64_t r4 = int64_t(4) * r;
-  const int64_t L1 = q + 1 - r4 <= 0 ? 0 : (q + 1 - r4 >= 4 ? 4 : q + 1 - r4);
-  const int64_t L0 = q - r4 <= 0 ? 0 : (q - r4 >= 4 ? 4 : q - r4);
-  const int64_t len = c < rem ? L1 : L0;
-  if (len == 0) return false;
-  const int64_t base = rem * (r4 < q + 1 ? r4 : q + 1) + (G - rem) * (r4 < q ? r4 : q);
-  const int64_t off = (c < rem ? c : rem) * L1 + (c > rem ? c - rem : 0) * L0;
-  const int64_t u0 = REV ? U - (base + off + len) : base + off;
-  row0 = u0 * kBoxRows;
-  rows = (T - row0) < len * kBoxRows ? (T - row0) : len * kBoxRows;
-  return true;
-}
-
 // COEFFS: the epilogue also runs K2 on each token's stored (bf16) logits and
 // writes h_pre, h_post and H_merged (k2_token.cuh), saving K2's launch and
 // its read of proj.
@@ -132,7 +100,7 @@ __device__ __forceinline__ bool fwd_tile(int64_t U, int64_t T, int r, int64_t &r
 // the other roles leave their loops, the producer's drain wait on the same
 // stage expires too (bounded), TMEM is freed and the CTA returns.  No copy is
 // left in flight.  The production instantiations have LOSE_COPY = false.
-template <bool COEFFS, bool LOSE_COPY = false, bool REV = true>
+template <bool COEFFS, bool LOSE_COPY = false>
 __global__ void __launch_bounds__(kThreads, FMHC_K1F_CTAS_PER_SM)
 k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
                  const __grid_constant__ CUtensorMap tmap_w, __nv_bfloat16 *__restrict__ out,
@@ -145,9 +113,12 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
   const int lane = threadIdx.x & 31;
   volatile int *abort = &sm.abort;
 
-  // This CTA's units (see fwd_tile): q or q + 1, taken up to 4 per round.
-  const int64_t my_units = units / gridDim.x + (int64_t(blockIdx.x) < units % gridDim.x ? 1 : 0);
-  const int ntiles = int((my_units + 3) / 4);
+  // Contiguous token range of this CTA, in 32-row units.
+  const int64_t u0 = int64_t(blockIdx.x) * units / gridDim.x;
+  const int64_t u1 = int64_t(blockIdx.x + 1) * units / gridDim.x;
+  const int64_t t_begin = u0 * kBoxRows;
+  const int64_t t_end = (u1 * kBoxRows < T) ? u1 * kBoxRows : T;
+  const int ntiles = t_end > t_begin ? int((t_end - t_begin + kBM - 1) / kBM) : 0;
   const int nk = nC / kBK;
 
   if (threadIdx.x == 0) {
@@ -185,8 +156,8 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
       uint32_t phase = 0;
       int issued = 0;
       for (int tile = 0; tile < ntiles && !*abort; ++tile) {
-        int64_t row0 = 0, rows = 0;
-        fwd_tile<REV>(units, T, tile, row0, rows);
+        const int64_t row0 = t_begin + int64_t(tile) * kBM;
+        const int64_t rows = (t_end - row0) < kBM ? (t_end - row0) : kBM;
         const int nbox = int((rows + kBoxRows - 1) / kBoxRows);
         for (int kb = 0; kb < nk; ++kb) {
           if (!mbar_wait(smem_u32(&sm.empty[stage]), phase ^ 1, abort, kSiteProdEmpty)) break;
@@ -262,8 +233,8 @@ k1_fwd_tc_kernel(const __grid_constant__ CUtensorMap tmap_x,
     int acc = 0;
     uint32_t acc_phase = 0;
     for (int tile = 0; tile < ntiles && !*abort; ++tile) {
-      int64_t row0 = 0, rows = 0;
-      fwd_tile<REV>(units, T, tile, row0, rows);
+      const int64_t row0 = t_begin + int64_t(tile) * kBM;
+      const int64_t rows = (t_end - row0) < kBM ? (t_end - row0) : kBM;
       // Eight independent partial sums (one per bf16 lane of a 16-byte chunk)
       // keep the FMA pipe busy instead of one serial chain per thread.
       float ss8[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
@@ -975,11 +946,7 @@ int launch_k1_tc_fwd(const void *x, const void *W, void *out, float *inv_rms, in
   int64_t grid = int64_t(device_sms()) * FMHC_K1F_CTAS_PER_SM;
   if (grid > units) grid = units;
   const size_t smem = sizeof(FwdSmem) + 1024;
-#ifndef FMHC_K1F_REV  // 0: the forward sweep (A/B measurements)
-#define FMHC_K1F_REV 1
-#endif
-  auto kern = coeffs ? k1_fwd_tc_kernel<true, false, FMHC_K1F_REV != 0>
-                     : k1_fwd_tc_kernel<false, false, FMHC_K1F_REV != 0>;
+  auto kern = coeffs ? k1_fwd_tc_kernel<true> : k1_fwd_tc_kernel<false>;
   if (int e = set_smem_attr(reinterpret_cast<const void *>(kern), smem)) return e;
   launch(kern, dim3(unsigned(grid)), dim3(kThreads), smem, s, mx, mw,
          reinterpret_cast<__nv_bfloat16 *>(out), inv_rms, T, nC, units, P, co);

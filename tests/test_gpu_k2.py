@@ -45,9 +45,13 @@ def test_k2_forward_matches_reference_eager_bf16(T, scale):
                                                       blk.alpha_res, blk.W_all.bias, blk.perm_mat)
     with torch.no_grad():
         r_pre, r_post, r_H = blk._coeffs_from_proj(proj, torch.bfloat16)
+    # The bf16 eager code rounds every op: H_merged = H_res - h_post h_pre
+    # subtracts two bf16-rounded terms of magnitude up to 1 and 2 (half-steps
+    # 2^-9 and 2^-8) computed from bf16-rounded sigmoids and softmax, so it is
+    # off the f32 value by up to ~3e-2 absolute.
     torch.testing.assert_close(h_pre, r_pre.float(), atol=1e-2, rtol=1e-2)
     torch.testing.assert_close(h_post, r_post.float(), atol=2e-2, rtol=1e-2)
-    torch.testing.assert_close(H, r_H.float(), atol=2e-2, rtol=2e-2)
+    torch.testing.assert_close(H, r_H.float(), atol=3e-2, rtol=2e-2)
     # f32 coefficients: the reference's K2 evaluated in float32 on the same
     # bf16 logits, with the parameters rounded to bf16 as its `.to(dt)` does
     with torch.no_grad():
