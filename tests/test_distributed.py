@@ -87,6 +87,22 @@ def _worker(rank, world, port, out_dir, mode):
         blk = _model(0)
         x, g = _data()
         xs, gs = shard_tokens(x, rank, world), shard_tokens(g, rank, world)
+        if mode == "bucketed_unused":
+            # a layer parameter the forward never uses gets no gradient: the
+            # layer bucket cannot complete in the hooks, so the block's own
+            # bucket (complete during backward) must wait for it, and finish()
+            # launches both in bucket order with zeros for the unused one
+            blk.layer.register_parameter("unused", nn.Parameter(torch.ones(3)))
+            red = BucketedGradReducer(blk)
+            (blk(xs) * gs).sum().backward()
+            assert red._next == 0  # nothing launched: the first bucket is incomplete
+            red.finish()
+            red.remove()
+            grads = {n: p.grad.clone() for n, p in blk.named_parameters()}
+            torch.save({"grads": grads}, os.path.join(out_dir, f"r{rank}.pt"))
+            dist.barrier()
+            dist.destroy_process_group()
+            return
         if mode == "bucketed":
             # two steps through the overlapped reducer: the hooks launch each
             # bucket during backward; the second step checks the state resets
@@ -144,14 +160,16 @@ def _reference_grads():
     return {n: p.grad.clone() for n, p in blk.named_parameters()}
 
 
-@pytest.mark.parametrize("mode", ["sum", "async", "avg", "bucketed"])
+@pytest.mark.parametrize("mode", ["sum", "async", "avg", "bucketed", "bucketed_unused"])
 def test_token_sharded_grads_equal_full_batch(mode):
     out_dir, procs = _run(mode)
     assert all(p.exitcode == 0 for p in procs)
     ref = _reference_grads()
-    scale = 0.5 if mode in ("avg", "bucketed") else 1.0
+    scale = 0.5 if mode in ("avg", "bucketed", "bucketed_unused") else 1.0
     for r in range(2):
         got = torch.load(os.path.join(out_dir, f"r{r}.pt"))["grads"]
+        if mode == "bucketed_unused":
+            assert torch.equal(got["layer.unused"], torch.zeros(3))
         for n, t in ref.items():
             torch.testing.assert_close(got[n], t * scale, atol=1e-5, rtol=1e-4, msg=n)
 
