@@ -81,6 +81,24 @@ def bytes_model(T: int, C: int, n: int = N_STREAMS, D: int = D_OUT) -> dict:
     }
 
 
+class _NoGC:
+    """Python's garbage collector off inside a timed region (collected just
+    before): a collection pause on one rank would otherwise stall that rank's
+    launches, and with a per-step collective the other ranks wait too."""
+
+    def __enter__(self):
+        import gc
+
+        gc.collect()
+        gc.disable()
+        return self
+
+    def __exit__(self, *exc):
+        import gc
+
+        gc.enable()
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -260,7 +278,10 @@ def _stepper(hp, torch, dist, world):
     if world == 1:
         return (lambda events=None: hp.step(hp.inputs, events)), (lambda: None)
     s_comm = torch.cuda.Stream()
-    pending = []  # the previous step's outputs, their grad_W not reduced yet
+    # The previous step's grad_W, not reduced yet.  Only grad_W is kept: holding
+    # the whole output set across steps would change the allocator's reuse of
+    # the (T, 4, C) output blocks (4 GiB each at configs[3]).
+    pending = []
 
     def launch_pending():
         if not pending:
@@ -275,7 +296,7 @@ def _stepper(hp, torch, dist, world):
 
     def one_step(events=None):
         outs = hp.step(hp.inputs, events, after_k4_fwd=launch_pending)
-        pending.append(outs)
+        pending.append({"gW": outs["gW"]})
         return outs
 
     def join_comm():
@@ -309,6 +330,15 @@ def run_ours(args):
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev,
                                 pg_options=opts)
 
+    if world > 1 and args.compute_priority == "high":
+        # Optional: this library's kernels (and the layer's) on a high-priority
+        # stream, NCCL's on its default-priority stream, so pending compute
+        # CTAs are dispatched before a collective's.  Backward nodes and the
+        # gradient hooks run on the stream of their forward, so this covers the
+        # block too.  Measured on 2 GPUs: no difference (block 3.50-3.51 ms
+        # either way), so it is off by default.
+        torch.cuda.set_stream(torch.cuda.Stream(priority=-1))
+
     T, C = args.T, args.C
     hp = HotPath(T, C, dev, seed=1234 + rank, torch=torch)
     lib_path = str(_native.library_path())
@@ -328,7 +358,7 @@ def run_ours(args):
     # `roofline`.  The clock sampler runs across both.
     events = {}
     phys = _physical_gpu_indices(world)
-    with ClockSampler(phys if rank == 0 else []) as clk:
+    with ClockSampler(phys if rank == 0 else []) as clk, _NoGC():
         torch.cuda.synchronize()
         if world > 1:
             dist.barrier()
@@ -357,7 +387,7 @@ def run_ours(args):
 
     # --- end-to-end from host buffers --------------------------------------
     e2e = None if args.no_e2e else run_e2e(args, hp, one_step, torch, dist, world, dev)
-    del hp
+    del hp, one_step, join_comm  # the step closures hold the inputs and last outputs
     torch.cuda.empty_cache()
 
     # --- the whole block ------------------------------
@@ -420,6 +450,12 @@ def run_ours(args):
             "tiny_inference": tiny,
             "gpu_launches": HotPath.LAUNCHES_PER_STEP * args.steps,
             "clocks": clk.summary(),
+            "comm": None if world == 1 else {
+                "grad_w_allreduce": "f32, on a side stream after the next step's K4 forward",
+                "block_grad_allreduce": "BucketedGradReducer (hooks, overlapped with backward)",
+                "compute_stream_priority": args.compute_priority,
+                "nccl_max_ctas": args.nccl_max_ctas or "default",
+                "nccl_nvls_ctas": args.nccl_nvls_ctas or "default"},
             "native_lib": os.path.relpath(lib_path, ROOT),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -595,11 +631,12 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
         dist.barrier()
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        step()
-    e.record()
-    torch.cuda.synchronize()
+    with _NoGC():
+        s.record()
+        for _ in range(steps):
+            step()
+        e.record()
+        torch.cuda.synchronize()
     ms = s.elapsed_time(e) / steps
     if world > 1:
         tt = torch.tensor([ms], device=dev)
@@ -638,12 +675,13 @@ def run_large(args, torch, dist, world, dev):
         dist.barrier()
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
-    s.record()
-    for _ in range(steps):
-        one_step()
-    join_comm()
-    e.record()
-    torch.cuda.synchronize()
+    with _NoGC():
+        s.record()
+        for _ in range(steps):
+            one_step()
+        join_comm()
+        e.record()
+        torch.cuda.synchronize()
     ms = s.elapsed_time(e) / steps
     if world > 1:
         tt = torch.tensor([ms], device=dev)
@@ -724,10 +762,11 @@ def run_e2e(args, hp, one_step, torch, dist, world, dev):
     t0 = time.perf_counter()
     start = torch.cuda.Event(enable_timing=True)
     end = torch.cuda.Event(enable_timing=True)
-    start.record(s_in)
-    run(steps)
-    end.record(s_out)
-    torch.cuda.synchronize()
+    with _NoGC():
+        start.record(s_in)
+        run(steps)
+        end.record(s_out)
+        torch.cuda.synchronize()
     ms = start.elapsed_time(end) / steps
     wall_ms = (time.perf_counter() - t0) * 1e3 / steps
     if world > 1:
@@ -1156,6 +1195,9 @@ def main():
                     help="skip the large token-sharded config (configs[3])")
     ap.add_argument("--large-T", type=int, default=131072, help="tokens per GPU, configs[3]")
     ap.add_argument("--large-C", type=int, default=4096)
+    ap.add_argument("--compute-priority", choices=["high", "default"], default="default",
+                    help="with N > 1: the stream priority of the compute stream (NCCL keeps "
+                         "the default priority)")
     ap.add_argument("--nccl-max-ctas", type=int, default=0,
                     help="NCCL communicator max_ctas (0: NCCL's default)")
     ap.add_argument("--nccl-nvls-ctas", type=int, default=0,

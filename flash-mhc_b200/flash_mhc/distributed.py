@@ -112,8 +112,9 @@ class BucketedGradReducer:
 
     Call ``finish()`` after ``backward()``: it launches any bucket still
     pending (parameters without a gradient count as zero), makes the current
-    stream wait for the reductions, scales by 1/world_size (``average``) and
-    writes the sums back into ``.grad`` with one multi-tensor copy per bucket.
+    stream wait for the reductions and writes the results back into ``.grad``
+    with one multi-tensor copy per bucket.  With ``average`` the result is the
+    mean over ranks (NCCL's AVG reduction; SUM and a scale on other backends).
     """
 
     def __init__(self, module: torch.nn.Module, buckets=None, group=None, average: bool = True,
@@ -142,6 +143,10 @@ class BucketedGradReducer:
                 self._index[id(p)] = bi
                 self._handles.append(p.register_post_accumulate_grad_hook(self._hook))
         self._next = 0  # first bucket not launched yet
+        # NCCL averages in the collective itself; other backends sum and the
+        # buffer is scaled in finish()
+        self._avg_in_collective = average and dist.get_backend(group) == "nccl"
+        self._op = dist.ReduceOp.AVG if self._avg_in_collective else dist.ReduceOp.SUM
 
     def _buffer(self, b, device):
         if b["buf"] is None:
@@ -163,7 +168,7 @@ class BucketedGradReducer:
             buf.zero_()
         if have:
             torch._foreach_copy_([v for v, _ in have], [g for _, g in have])
-        b["work"] = dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=self.group, async_op=True)
+        b["work"] = dist.all_reduce(buf, op=self._op, group=self.group, async_op=True)
 
     def _launch_ready(self):
         while self._next < len(self.buckets):
@@ -184,7 +189,7 @@ class BucketedGradReducer:
         world = dist.get_world_size(self.group)
         for b in self.buckets:
             b["work"].wait()
-            if self.average and world > 1:
+            if self.average and world > 1 and not self._avg_in_collective:
                 b["buf"].mul_(1.0 / world)
             grads = []
             for p, v in zip(b["params"], b["views"]):

@@ -241,8 +241,10 @@ FMHC_API int fmhc_mhc_grad_x_combine_post(const void *gx1, const void *grad_li,
  *   a      = softmax(a_res * proj[:, 8:32] + bias[8:32])
  *   H_merged[i][j] = sum_k a[k] perm[k][4i+j] - h_post[i] h_pre[j]
  * proj (T, 32) bf16; params (35,) f32 = [a_pre, a_post, a_res, bias[32]];
- * perm (24, 16) f32 -> h_pre, h_post (T, 4) f32, H_merged (T, 4, 4) f32, each
- * rounded to bf16 like the reference (which computes K2 in the input dtype).
+ * perm (24, 16) f32 -> h_pre, h_post (T, 4) f32, H_merged (T, 4, 4) f32.  The
+ * parameters are rounded to bf16 as the reference's .to(dt) does; the
+ * arithmetic and the outputs are f32 (the reference's bf16 eager K2 rounds
+ * every op; f32 keeps the block within 2e-2 / 1e-2 of its float32 path).
  * Replaces the eager K2 of the caller (src/flash_mhc/block.py:150-170),
  * ~20 torch launches.
  */
