@@ -99,6 +99,18 @@ class _NoGC:
         gc.enable()
 
 
+def _launch_lead(torch, ms):
+    """Keep the GPU busy for ``ms`` (a fixed-length sleep kernel on the current
+    stream, bounded by construction) before a timed region's start event, so the
+    host can enqueue the region's launches before the GPU reaches them: a host
+    stall on one rank (shared host CPUs, NCCL's helper threads) then no longer
+    drains that rank's queue, which with a per-step collective would stall every
+    rank.  The sleep itself is outside the timed events.  (nvbench's blocking
+    kernel serves the same purpose.)"""
+    if ms > 0:
+        torch.cuda._sleep(int(ms * 2.0e6))  # ~2 GHz SM clock: cycles per ms
+
+
 def measured_peaks() -> dict:
     p = ROOT / "MEASURED_PEAKS.json"
     if p.exists():
@@ -364,6 +376,7 @@ def run_ours(args):
             dist.barrier()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
+        _launch_lead(torch, args.launch_lead_ms)
         t0.record()
         for _ in range(args.steps):
             one_step()
@@ -452,7 +465,7 @@ def run_ours(args):
             "clocks": clk.summary(),
             "comm": None if world == 1 else {
                 "grad_w_allreduce": "f32, on a side stream after the next step's K4 forward",
-                "block_grad_allreduce": "BucketedGradReducer (hooks, overlapped with backward)",
+                "block_grad_allreduce": f"BucketedGradReducer, {args.block_buckets} bucket(s)",
                 "compute_stream_priority": args.compute_priority,
                 "nccl_max_ctas": args.nccl_max_ctas or "default",
                 "nccl_nvls_ctas": args.nccl_nvls_ctas or "default"},
@@ -613,7 +626,12 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
         layer.weight.copy_((torch.randn(C, C, generator=g, device=dev) * 0.02).bfloat16())
     x = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16().requires_grad_(True)
     up = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16()
-    reducer = BucketedGradReducer(blk) if world > 1 else None
+    reducer = None
+    if world > 1:
+        # 2: the layer's bucket reduces during the backward, the block's own at
+        # its end; 1: one bucket, reduced when the last gradient arrives
+        reducer = BucketedGradReducer(
+            blk, buckets=None if args.block_buckets == 2 else [list(blk.parameters())])
 
     def step():
         blk.zero_grad(set_to_none=True)
@@ -632,6 +650,7 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
     with _NoGC():
+        _launch_lead(torch, args.launch_lead_ms)
         s.record()
         for _ in range(steps):
             step()
@@ -649,8 +668,10 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
                                                "(configs[2])",
                        "T_per_gpu": T, "C": C, "n": N_STREAMS,
                        "layer": f"nn.Linear({C}, {C}, bias=False) ~N(0,0.02)",
-                       "grad_allreduce": "bucketed, overlapped with the backward" if world > 1
-                       else "none (1 GPU)"},
+                       "grad_allreduce": ("none (1 GPU)" if world == 1 else
+                                          "BucketedGradReducer: layer bucket during the backward, "
+                                          "block's own at its end" if args.block_buckets == 2 else
+                                          "BucketedGradReducer: one bucket at the end of the backward")},
             "value": round(world * T / (ms * 1e-3), 1), "unit": UNIT, "ms_per_step": round(ms, 4),
             "steps": steps, "layer_gemm_tflops_per_step": round(flops / 1e12, 3)}
 
@@ -676,6 +697,7 @@ def run_large(args, torch, dist, world, dev):
     s = torch.cuda.Event(enable_timing=True)
     e = torch.cuda.Event(enable_timing=True)
     with _NoGC():
+        _launch_lead(torch, args.launch_lead_ms)
         s.record()
         for _ in range(steps):
             one_step()
@@ -1195,6 +1217,10 @@ def main():
                     help="skip the large token-sharded config (configs[3])")
     ap.add_argument("--large-T", type=int, default=131072, help="tokens per GPU, configs[3]")
     ap.add_argument("--large-C", type=int, default=4096)
+    ap.add_argument("--launch-lead-ms", type=float, default=20.0,
+                    help="GPU sleep before each timed region's start event (0: none)")
+    ap.add_argument("--block-buckets", type=int, choices=[1, 2], default=2,
+                    help="with N > 1: gradient buckets of the block's all-reduce")
     ap.add_argument("--compute-priority", choices=["high", "default"], default="default",
                     help="with N > 1: the stream priority of the compute stream (NCCL keeps "
                          "the default priority)")
