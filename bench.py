@@ -18,7 +18,12 @@ all-reduced over NCCL, the path's only exchange.
 * ``value``: whole-job tokens/s with inputs resident in HBM (max step time over
   ranks, CUDA events on the launching stream at the ends of the timed region).
   Inputs (x alone is 512 MiB) exceed the 126 MB L2, so no flush is needed
-  between steps.
+  between steps.  Each timed region starts after a barrier and a synchronize,
+  then a fixed-length GPU sleep (``--launch-lead-ms``, outside the events) so
+  the host can enqueue the region before the GPU reaches it; Python's garbage
+  collector is off inside it.  With N > 1 the grad_W all-reduce of step i runs
+  on a side stream after step i+1's K4 forward; ``per_gpu`` carries the
+  per-GPU figure (BASELINE's metric name says "per GPU").
 * ``roofline``: the dominant kernel (K4 backward) -- algorithmic bytes per
   launch (the reference's bytes model, scripts/benchmark_kernels.py:64-105)
   over its CUDA-event duration, measured in a second timed region of the same
@@ -36,6 +41,13 @@ all-reduced over NCCL, the path's only exchange.
   full per-GPU batch (T tokens) per step, rank 0 only.  Where
   ``baseline/_ref`` is missing it falls back to the float32 numpy
   restatement under ``oracle/`` (``kind: "port"``).
+* ``block``: ``MHCLiteBlock`` fwd+bwd at BASELINE configs[2] (T=65536 per GPU,
+  C=2048, Linear(2048, 2048)); with N > 1 its gradients are all-reduced by
+  ``flash_mhc.distributed.BucketedGradReducer`` during the backward.
+* ``large``: BASELINE configs[3] per GPU (131,072 tokens, C=4096): the hot-path
+  step and the block with the 4096 -> 4096 linear, at every N.
+* ``small_batch_graphs`` / ``tiny_inference``: the hot path at T=8192 eager vs
+  CUDA-graph replay, and the no-grad block forward at T=1/16/256.
 * ``--impl reference-triton``: a comparison line, not the reference arm -- the
   unmodified reference's Triton kernels and block, installed in
   ``baseline/_ref``, timed on this GPU on the same shapes and seeds.
