@@ -351,6 +351,8 @@ def run_ours(args):
             opts.config.max_ctas = args.nccl_max_ctas
         if args.nccl_nvls_ctas > 0:
             opts.config.nvls_ctas = args.nccl_nvls_ctas
+        if args.nccl_cta_policy >= 0:
+            opts.config.cta_policy = args.nccl_cta_policy
         dist.init_process_group("nccl", timeout=timedelta(seconds=120), device_id=dev,
                                 pg_options=opts)
 
@@ -477,10 +479,14 @@ def run_ours(args):
             "clocks": clk.summary(),
             "comm": None if world == 1 else {
                 "grad_w_allreduce": "f32, on a side stream after the next step's K4 forward",
-                "block_grad_allreduce": f"BucketedGradReducer, {args.block_buckets} bucket(s)",
+                "block_grad_allreduce": (f"BucketedGradReducer, {args.block_buckets} bucket(s), "
+                                         f"{args.block_reduce_op}"
+                                         if args.block_allreduce == "bucketed" else
+                                         "allreduce_gradients: one bucket after the backward"),
                 "compute_stream_priority": args.compute_priority,
                 "nccl_max_ctas": args.nccl_max_ctas or "default",
-                "nccl_nvls_ctas": args.nccl_nvls_ctas or "default"},
+                "nccl_nvls_ctas": args.nccl_nvls_ctas or "default",
+                "nccl_cta_policy": args.nccl_cta_policy if args.nccl_cta_policy >= 0 else "default"},
             "native_lib": os.path.relpath(lib_path, ROOT),
         }
         if world == 1 and not args.no_cpu_baseline:
@@ -625,7 +631,7 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
     import torch.nn as nn
 
     from flash_mhc import MHCLiteBlock
-    from flash_mhc.distributed import BucketedGradReducer
+    from flash_mhc.distributed import BucketedGradReducer, allreduce_gradients
 
     T = T or args.block_T
     C = C or args.block_C
@@ -639,11 +645,12 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
     x = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16().requires_grad_(True)
     up = torch.randn(T, N_STREAMS, C, generator=g, device=dev).bfloat16()
     reducer = None
-    if world > 1:
+    if world > 1 and args.block_allreduce == "bucketed":
         # 2: the layer's bucket reduces during the backward, the block's own at
         # its end; 1: one bucket, reduced when the last gradient arrives
         reducer = BucketedGradReducer(
-            blk, buckets=None if args.block_buckets == 2 else [list(blk.parameters())])
+            blk, buckets=None if args.block_buckets == 2 else [list(blk.parameters())],
+            avg_op=args.block_reduce_op == "avg")
 
     def step():
         blk.zero_grad(set_to_none=True)
@@ -652,6 +659,8 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
         out.backward(up)
         if reducer is not None:
             reducer.finish()
+        elif world > 1:
+            allreduce_gradients(blk)  # one f32 bucket after the backward
 
     steps = max(1, min(args.steps, 10))
     for _ in range(max(3, min(args.warmup, 5))):
@@ -681,6 +690,8 @@ def run_block(args, torch, dist, world, dev, T=None, C=None, workload=None):
                        "T_per_gpu": T, "C": C, "n": N_STREAMS,
                        "layer": f"nn.Linear({C}, {C}, bias=False) ~N(0,0.02)",
                        "grad_allreduce": ("none (1 GPU)" if world == 1 else
+                                          "allreduce_gradients: one f32 bucket after the backward"
+                                          if args.block_allreduce == "after" else
                                           "BucketedGradReducer: layer bucket during the backward, "
                                           "block's own at its end" if args.block_buckets == 2 else
                                           "BucketedGradReducer: one bucket at the end of the backward")},
@@ -1231,6 +1242,11 @@ def main():
     ap.add_argument("--large-C", type=int, default=4096)
     ap.add_argument("--launch-lead-ms", type=float, default=20.0,
                     help="GPU sleep before each timed region's start event (0: none)")
+    ap.add_argument("--block-allreduce", choices=["bucketed", "after"], default="bucketed",
+                    help="with N > 1: BucketedGradReducer, or one bucket after the backward "
+                         "(allreduce_gradients)")
+    ap.add_argument("--block-reduce-op", choices=["sum", "avg"], default="sum",
+                    help="with N > 1: NCCL SUM + scale, or NCCL AVG, for the block's gradients")
     ap.add_argument("--block-buckets", type=int, choices=[1, 2], default=2,
                     help="with N > 1: gradient buckets of the block's all-reduce")
     ap.add_argument("--compute-priority", choices=["high", "default"], default="default",
@@ -1238,6 +1254,8 @@ def main():
                          "the default priority)")
     ap.add_argument("--nccl-max-ctas", type=int, default=0,
                     help="NCCL communicator max_ctas (0: NCCL's default)")
+    ap.add_argument("--nccl-cta-policy", type=int, default=-1,
+                    help="NCCL communicator cta_policy (-1: NCCL's default)")
     ap.add_argument("--nccl-nvls-ctas", type=int, default=0,
                     help="NCCL communicator nvls_ctas (0: NCCL's default)")
     args = ap.parse_args()

@@ -114,11 +114,12 @@ class BucketedGradReducer:
     pending (parameters without a gradient count as zero), makes the current
     stream wait for the reductions and writes the results back into ``.grad``
     with one multi-tensor copy per bucket.  With ``average`` the result is the
-    mean over ranks (NCCL's AVG reduction; SUM and a scale on other backends).
+    mean over ranks: a SUM all-reduce and a scale, or with ``avg_op`` (NCCL
+    only) NCCL's AVG reduction.
     """
 
     def __init__(self, module: torch.nn.Module, buckets=None, group=None, average: bool = True,
-                 reduce_dtype: torch.dtype = torch.float32):
+                 reduce_dtype: torch.dtype = torch.float32, avg_op: bool = False):
         self.group = group
         self.average = average
         self.reduce_dtype = reduce_dtype
@@ -143,9 +144,9 @@ class BucketedGradReducer:
                 self._index[id(p)] = bi
                 self._handles.append(p.register_post_accumulate_grad_hook(self._hook))
         self._next = 0  # first bucket not launched yet
-        # NCCL averages in the collective itself; other backends sum and the
-        # buffer is scaled in finish()
-        self._avg_in_collective = average and dist.get_backend(group) == "nccl"
+        # avg_op: NCCL averages in the collective itself; otherwise (and on
+        # other backends) the buckets are summed and scaled in finish()
+        self._avg_in_collective = avg_op and average and dist.get_backend(group) == "nccl"
         self._op = dist.ReduceOp.AVG if self._avg_in_collective else dist.ReduceOp.SUM
 
     def _buffer(self, b, device):
